@@ -1,0 +1,161 @@
+/*
+ * pytorch_opt_b200 — C ABI of the B200-native (sm_100a) numerics behind
+ * pytorch_opt.ops.
+ *
+ * Every entry point takes plain device pointers, element counts and strides
+ * (in elements), a caller-provided device workspace, and a cudaStream_t passed
+ * as `void*` (NULL = legacy default stream). Nothing here allocates device
+ * memory; query the workspace size first with the matching *_workspace_bytes
+ * function and pass at least that many bytes.
+ *
+ * Return value: PO_OK (0) or a PO_ERR_* code; po_last_error() then holds a
+ * message for the calling thread. Kernels never trap: a bounded wait that
+ * gives up records a code in the device error word, read with
+ * po_device_error().
+ *
+ * Layout convention: a "matrix batch" is [batch][rows][cols], row-major with
+ * row pitch `ld` and batch pitch `bstride`; columns are contiguous.
+ */
+#ifndef PYTORCH_OPT_B200_H_
+#define PYTORCH_OPT_B200_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define PO_F32 0
+#define PO_BF16 1
+#define PO_F16 2
+#define PO_F64 3
+
+/* status codes */
+#define PO_OK 0
+#define PO_ERR_ARG 1         /* invalid argument (shape, dtype, stride, value) */
+#define PO_ERR_CUDA 2        /* a CUDA runtime / driver call failed */
+#define PO_ERR_WORKSPACE 3   /* workspace too small */
+#define PO_ERR_DEVICE 4      /* a kernel recorded an error in the device error word */
+#define PO_ERR_UNSUPPORTED 5 /* valid request this build does not implement */
+
+/* Message describing the last failure on the calling thread ("" if none). */
+const char* po_last_error(void);
+
+/* Synchronises the current device, returns the device error word (0 = none)
+ * and clears it when `reset` is nonzero. */
+int po_device_error(int reset);
+
+/* Library version string. */
+const char* po_version(void);
+
+/* ------------------------------------------------------------------------
+ * Newton–Schulz orthogonalisation.
+ * Replaces pytorch_opt/ops/csrc/pytorch_opt_ops.cpp:65-81
+ * (newton_schulz_orthogonalize(G, steps, a, b, c, eps), bound at :106) and
+ * mirrors pytorch_opt/ops/reference.py:71-97: transpose when rows > cols,
+ * divide by (||X||_F + eps), `steps` quintic iterations
+ * A = X X^T, B = b A + c A^2, X = a X + B X, transpose back, cast to the
+ * input dtype. G and out: [batch][rows][cols] of `dtype`
+ * (PO_F32 / PO_BF16 / PO_F16 / PO_F64). The first (steps - tf32_tail)
+ * iterations run bf16 tensor-core products, the last `tf32_tail` run tf32
+ * products, all accumulating in fp32. tf32_tail < 0 selects the default:
+ * 2 when min(rows, cols) >= 512, else all steps.
+ * ---------------------------------------------------------------------- */
+size_t po_ns_workspace_bytes(long long batch, long long rows, long long cols);
+int po_newton_schulz(const void* G, int dtype, long long batch, long long rows, long long cols, long long ld,
+                     long long bstride, void* out, long long out_ld, long long out_bstride, int steps, float a,
+                     float b, float c, float eps, int tf32_tail, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* ------------------------------------------------------------------------
+ * Inverse p-th root (A_sym + damping I)^(-1/p) by the coupled Newton
+ * iteration. Replaces pytorch_opt/ops/csrc/pytorch_opt_ops.cpp:15-39 and
+ * :41-63 for method="newton" (bound at :104) and mirrors
+ * pytorch_opt/ops/reference.py:17-40 and :43-68: symmetrise, add damping,
+ * z = (1+p)/(2||M||_F), X0 = z^(1/p) I, M0 = z M, iterate
+ * Mi = (1+1/p) I - Mk/p, X <- X Mi, Mk <- Mi^p Mk until max|Mk - I| < tol,
+ * or it grows by more than 1.2x (then the previous X is kept), or max_iter;
+ * finally symmetrise and cast back. Products run on the tensor cores as
+ * split-bf16 (hi*hi + hi*lo + lo*hi, fp32 accumulate) while max|Mk - I| >
+ * 1e-3 and as single bf16 afterwards; the iteration is carried in the
+ * increment form E = Mk - I so that the stopping test sees the same values
+ * as the fp64 reference. No host synchronisation happens inside.
+ * A and out: [batch][d][d] of `dtype` (PO_F32 / PO_BF16 / PO_F64).
+ * iters_out (nullable): device int[batch], iterations each item ran.
+ * ---------------------------------------------------------------------- */
+size_t po_root_workspace_bytes(long long batch, long long d, int p);
+int po_inverse_root(const void* A, int dtype, long long batch, long long d, long long ld, long long bstride,
+                    void* out, long long out_ld, long long out_bstride, int p, double damping, int max_iter,
+                    double tol, int* iters_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * In-place Kronecker factor update. Replaces
+ * pytorch_opt/ops/csrc/pytorch_opt_ops.cpp:83-94 (bound at :108) and mirrors
+ * pytorch_opt/ops/reference.py:100-114:
+ *   L <- beta2 L + (1 - beta2) G G^T,  R <- beta2 R + (1 - beta2) G^T G
+ * (beta2 == 1: plain sums). G: m x n (row pitch g_ld) of g_dtype
+ * (PO_F32 / PO_BF16); L (m x m, pitch l_ld) and R (n x n, pitch r_ld) are
+ * fp32. Only the lower triangle of tiles is computed; the upper triangle is
+ * written by mirroring. fp32 G uses split-bf16 products.
+ * ---------------------------------------------------------------------- */
+size_t po_kron_workspace_bytes(long long m, long long n, int g_dtype);
+int po_kron_factor_update(float* L, long long l_ld, float* R, long long r_ld, const void* G, int g_dtype,
+                          long long m, long long n, long long g_ld, double beta2, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * KFAC factor statistics with the exponential moving average fused:
+ *   F <- first ? S : beta F + (1 - beta) S,   S = alpha * X^T X
+ * X: rows x d (pitch x_ld) of x_dtype (PO_F32 / PO_BF16); F: d x d fp32.
+ * Replaces pytorch_opt/curvature/kron.py:105-113 (_batch_factors, Linear:
+ * A = a^T a / n with alpha = 1/n; G = ghat^T ghat / n with ghat = n g, i.e.
+ * alpha = n) together with the EMA of kron.py:95-103 (first call clones).
+ * ---------------------------------------------------------------------- */
+size_t po_syrk_workspace_bytes(long long rows, long long d, int x_dtype);
+int po_syrk_ema(float* F, long long d, long long f_ld, const void* X, int x_dtype, long long rows, long long x_ld,
+                double alpha, double beta, int first, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Two-sided preconditioner application out = L @ G @ R. Replaces
+ * pytorch_opt/ops/csrc/pytorch_opt_ops.cpp:96-99 (bound at :110) and mirrors
+ * pytorch_opt/ops/reference.py:117-121. All operands fp32 (or all bf16):
+ * L m x m, G m x n, R n x n, out m x n, dense row-major with the given
+ * pitches. fp32 operands use split-bf16 products.
+ * ---------------------------------------------------------------------- */
+size_t po_precond_workspace_bytes(long long m, long long n, int dtype);
+int po_precond_apply(const void* L, long long l_ld, const void* G, long long g_ld, const void* R, long long r_ld,
+                     void* out, long long out_ld, int dtype, long long m, long long n, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Elementwise halves of the Muon step, flat over n elements of `dtype`
+ * (PO_F32 / PO_BF16), rounding after each in-place op like the reference's
+ * pytorch_opt/optim/muon.py:82-83 and :87-92.
+ *   po_muon_momentum: buf <- buf*momentum + g; u <- nesterov ? g + momentum*buf : buf
+ *   po_muon_apply:    p <- p*decay (when decay != 1); p <- p - lr_eff*o;
+ *                     *sq_sum (device fp64, nullable) += sum(o^2)
+ * ---------------------------------------------------------------------- */
+int po_muon_momentum(const void* g, void* buf, void* u, int dtype, long long n, float momentum, int nesterov,
+                     void* stream);
+int po_muon_apply(void* p, const void* o, int dtype, long long n, float lr_eff, float decay, double* sq_sum,
+                  void* stream);
+
+/* ------------------------------------------------------------------------
+ * General batched product used by the ops above, exported for tests:
+ *   C[b] = alpha * op(A[b]) @ op(B[b]) + beta * C[b]
+ * A: M x K (trans_a: stored K x M), B: K x N (trans_b: stored N x K), all of
+ * `dtype` PO_BF16 (bf16 products) or PO_F32 (precision: 0 = tf32,
+ * 1 = split-bf16). C is fp32. Pitches in elements.
+ * ---------------------------------------------------------------------- */
+size_t po_matmul_workspace_bytes(long long batch, long long M, long long N, long long K, int dtype, int precision);
+int po_matmul(const void* A, long long lda, long long sa, int trans_a, const void* B, long long ldb, long long sb,
+              int trans_b, float* C, long long ldc, long long sc, int dtype, int precision, long long batch,
+              long long M, long long N, long long K, float alpha, float beta, void* workspace,
+              size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PYTORCH_OPT_B200_H_ */

@@ -1,0 +1,243 @@
+// Bandwidth-bound helper kernels (see elementwise.cuh).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "elementwise.cuh"
+#include "gemm.cuh"
+
+namespace po {
+
+template <int DT>
+struct Elem;
+template <>
+struct Elem<PO_F32> {
+  using T = float;
+  __device__ static double ld(const void* p, long long i) { return static_cast<const float*>(p)[i]; }
+};
+template <>
+struct Elem<PO_BF16> {
+  using T = __nv_bfloat16;
+  __device__ static double ld(const void* p, long long i) {
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  }
+};
+template <>
+struct Elem<PO_F16> {
+  using T = __half;
+  __device__ static double ld(const void* p, long long i) { return __half2float(static_cast<const __half*>(p)[i]); }
+};
+template <>
+struct Elem<PO_F64> {
+  using T = double;
+  __device__ static double ld(const void* p, long long i) { return static_cast<const double*>(p)[i]; }
+};
+
+__device__ __forceinline__ double block_sum(double v) {
+  __shared__ double part[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) part[w] = v;
+  __syncthreads();
+  double t = 0.0;
+  if (w == 0) {
+    t = (l < static_cast<int>(blockDim.x >> 5)) ? part[l] : 0.0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  }
+  return t;  // valid in thread 0
+}
+
+// ------------------------------------------------------------------ sumsq
+template <int DT>
+__global__ void sumsq_kernel(AnyMat M, double* sums) {
+  const int b = blockIdx.y;
+  double acc = 0.0;
+  for (long long r = blockIdx.x; r < M.rows; r += gridDim.x) {
+    const long long base = b * M.bstride + r * M.ld;
+    for (long long c = threadIdx.x; c < M.cols; c += blockDim.x) {
+      const double v = Elem<DT>::ld(M.ptr, base + c);
+      acc += v * v;
+    }
+  }
+  acc = block_sum(acc);
+  if (threadIdx.x == 0) atomicAdd(sums + b, acc);
+}
+
+int launch_sumsq(const AnyMat& M, int batch, double* sums, cudaStream_t s) {
+  if (M.rows <= 0 || M.cols <= 0 || batch <= 0) return PO_OK;
+  const int per = static_cast<int>(M.rows < 4LL * sm_count() ? M.rows : 4LL * sm_count());
+  const int blocks = batch >= 16 ? (per + 7) / 8 : per;
+  dim3 grid(blocks > 0 ? blocks : 1, batch);
+  switch (M.dtype) {
+    case PO_F32: sumsq_kernel<PO_F32><<<grid, 256, 0, s>>>(M, sums); break;
+    case PO_BF16: sumsq_kernel<PO_BF16><<<grid, 256, 0, s>>>(M, sums); break;
+    case PO_F16: sumsq_kernel<PO_F16><<<grid, 256, 0, s>>>(M, sums); break;
+    case PO_F64: sumsq_kernel<PO_F64><<<grid, 256, 0, s>>>(M, sums); break;
+    default: return set_error(PO_ERR_ARG, "sumsq: unsupported dtype");
+  }
+  return check_cuda(cudaGetLastError(), "sumsq launch");
+}
+
+// --------------------------------------------------------------- ns_pack
+// One 32x32 output tile per block (32 x 8 threads). Output element (r, c)
+// comes from src(c, r) when TRANS.
+template <int DT, bool TRANS>
+__global__ void ns_pack_kernel(AnyMat src, const double* sums, float eps, float* xf, void* xop, int op_kind,
+                               long long ldx, long long rows_out, long long cols_out) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const long long r0 = static_cast<long long>(blockIdx.y) * 32, c0 = static_cast<long long>(blockIdx.x) * 32;
+  const float den = static_cast<float>(sqrt(sums[b])) + eps;
+  const long long sbase = b * src.bstride;
+  if (TRANS) {
+    // src rows = output columns: read src(c0 + i, r0 + threadIdx.x) coalesced along r.
+    for (int i = threadIdx.y; i < 32; i += 8) {
+      const long long sr = c0 + i, sc = r0 + threadIdx.x;
+      float v = 0.0f;
+      if (sr < cols_out && sc < rows_out) v = static_cast<float>(Elem<DT>::ld(src.ptr, sbase + sr * src.ld + sc));
+      tile[i][threadIdx.x] = v;
+    }
+    __syncthreads();
+  }
+  const long long xbase = b * rows_out * ldx;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const long long r = r0 + i, c = c0 + threadIdx.x;
+    if (r >= rows_out || c >= cols_out) continue;
+    float v = TRANS ? tile[threadIdx.x][i] : static_cast<float>(Elem<DT>::ld(src.ptr, sbase + r * src.ld + c));
+    v = __fdiv_rn(v, den);
+    const long long o = xbase + r * ldx + c;
+    xf[o] = v;
+    if (op_kind == OUT_BF16) static_cast<__nv_bfloat16*>(xop)[o] = __float2bfloat16_rn(v);
+    else static_cast<float*>(xop)[o] = round_tf32(v);
+  }
+}
+
+template <int DT>
+static void ns_pack_dt(const AnyMat& src, int batch, bool trans, const double* sums, float eps, float* xf, void* xop,
+                       int op_kind, long long ldx, long long rows_out, long long cols_out, cudaStream_t s) {
+  dim3 grid(cdiv(cols_out, 32), cdiv(rows_out, 32), batch), block(32, 8);
+  if (trans) ns_pack_kernel<DT, true><<<grid, block, 0, s>>>(src, sums, eps, xf, xop, op_kind, ldx, rows_out, cols_out);
+  else ns_pack_kernel<DT, false><<<grid, block, 0, s>>>(src, sums, eps, xf, xop, op_kind, ldx, rows_out, cols_out);
+}
+
+int launch_ns_pack(const AnyMat& src, int batch, bool trans, const double* sums, float eps, float* xf, void* xop,
+                   int op_kind, long long ldx, long long rows_out, long long cols_out, cudaStream_t s) {
+  if (rows_out <= 0 || cols_out <= 0 || batch <= 0) return PO_OK;
+  switch (src.dtype) {
+    case PO_F32: ns_pack_dt<PO_F32>(src, batch, trans, sums, eps, xf, xop, op_kind, ldx, rows_out, cols_out, s); break;
+    case PO_BF16: ns_pack_dt<PO_BF16>(src, batch, trans, sums, eps, xf, xop, op_kind, ldx, rows_out, cols_out, s); break;
+    case PO_F16: ns_pack_dt<PO_F16>(src, batch, trans, sums, eps, xf, xop, op_kind, ldx, rows_out, cols_out, s); break;
+    case PO_F64: ns_pack_dt<PO_F64>(src, batch, trans, sums, eps, xf, xop, op_kind, ldx, rows_out, cols_out, s); break;
+    default: return set_error(PO_ERR_ARG, "ns_pack: unsupported dtype");
+  }
+  return check_cuda(cudaGetLastError(), "ns_pack launch");
+}
+
+// --------------------------------------------------------------- copy_out
+__device__ __forceinline__ void store_any(void* p, int dt, long long i, float v) {
+  switch (dt) {
+    case PO_F32: static_cast<float*>(p)[i] = v; break;
+    case PO_BF16: static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v); break;
+    case PO_F16: static_cast<__half*>(p)[i] = __float2half_rn(v); break;
+    default: static_cast<double*>(p)[i] = static_cast<double>(v); break;
+  }
+}
+
+// out (rows x cols, or cols x rows when TRANS) from src rows x cols.
+template <bool TRANS>
+__global__ void copy_out_kernel(const float* src, long long ld_src, long long bs_src, long long rows, long long cols,
+                                void* out, int out_dtype, long long ld_out, long long bs_out) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const long long r0 = static_cast<long long>(blockIdx.y) * 32, c0 = static_cast<long long>(blockIdx.x) * 32;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const long long r = r0 + i, c = c0 + threadIdx.x;
+    float v = 0.0f;
+    if (r < rows && c < cols) v = src[b * bs_src + r * ld_src + c];
+    if (!TRANS) {
+      if (r < rows && c < cols) store_any(out, out_dtype, b * bs_out + r * ld_out + c, v);
+    } else {
+      tile[i][threadIdx.x] = v;
+    }
+  }
+  if (TRANS) {
+    __syncthreads();
+    // out(c, r) = src(r, c): write rows c0.. of out, coalesced along r.
+    for (int i = threadIdx.y; i < 32; i += 8) {
+      const long long oc = c0 + i, orr = r0 + threadIdx.x;
+      if (oc < cols && orr < rows) store_any(out, out_dtype, b * bs_out + oc * ld_out + orr, tile[threadIdx.x][i]);
+    }
+  }
+}
+
+int launch_copy_out(const float* src, long long ld_src, long long bs_src, int batch, long long rows, long long cols,
+                    bool trans, void* out, int out_dtype, long long ld_out, long long bs_out, cudaStream_t s) {
+  if (rows <= 0 || cols <= 0 || batch <= 0) return PO_OK;
+  dim3 grid(cdiv(cols, 32), cdiv(rows, 32), batch), block(32, 8);
+  if (trans) copy_out_kernel<true><<<grid, block, 0, s>>>(src, ld_src, bs_src, rows, cols, out, out_dtype, ld_out, bs_out);
+  else copy_out_kernel<false><<<grid, block, 0, s>>>(src, ld_src, bs_src, rows, cols, out, out_dtype, ld_out, bs_out);
+  return check_cuda(cudaGetLastError(), "copy_out launch");
+}
+
+// ---------------------------------------------------------------- convert
+template <int DT>
+__global__ void convert_kernel(AnyMat src, void* dst, int dst_dtype, long long ld_dst, long long bs_dst) {
+  const int b = blockIdx.y;
+  for (long long r = blockIdx.x; r < src.rows; r += gridDim.x) {
+    const long long sb = b * src.bstride + r * src.ld, db = b * bs_dst + r * ld_dst;
+    for (long long c = threadIdx.x; c < src.cols; c += blockDim.x) {
+      const float v = static_cast<float>(Elem<DT>::ld(src.ptr, sb + c));
+      if (dst_dtype == PO_F32) static_cast<float*>(dst)[db + c] = v;
+      else static_cast<__nv_bfloat16*>(dst)[db + c] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+int launch_convert(const AnyMat& src, int batch, void* dst, int dst_dtype, long long ld_dst, long long bs_dst,
+                   cudaStream_t s) {
+  if (src.rows <= 0 || src.cols <= 0 || batch <= 0) return PO_OK;
+  if (dst_dtype != PO_F32 && dst_dtype != PO_BF16) return set_error(PO_ERR_ARG, "convert: bad destination dtype");
+  const int per = static_cast<int>(src.rows < 8LL * sm_count() ? src.rows : 8LL * sm_count());
+  dim3 grid(per, batch);
+  switch (src.dtype) {
+    case PO_F32: convert_kernel<PO_F32><<<grid, 256, 0, s>>>(src, dst, dst_dtype, ld_dst, bs_dst); break;
+    case PO_BF16: convert_kernel<PO_BF16><<<grid, 256, 0, s>>>(src, dst, dst_dtype, ld_dst, bs_dst); break;
+    case PO_F16: convert_kernel<PO_F16><<<grid, 256, 0, s>>>(src, dst, dst_dtype, ld_dst, bs_dst); break;
+    case PO_F64: convert_kernel<PO_F64><<<grid, 256, 0, s>>>(src, dst, dst_dtype, ld_dst, bs_dst); break;
+    default: return set_error(PO_ERR_ARG, "convert: unsupported dtype");
+  }
+  return check_cuda(cudaGetLastError(), "convert launch");
+}
+
+// ------------------------------------------------------------- split bf16
+template <int DT>
+__global__ void split_kernel(AnyMat src, __nv_bfloat16* hi, __nv_bfloat16* lo, long long ld_dst, long long bs_dst) {
+  const int b = blockIdx.y;
+  for (long long r = blockIdx.x; r < src.rows; r += gridDim.x) {
+    const long long sb = b * src.bstride + r * src.ld, db = b * bs_dst + r * ld_dst;
+    for (long long c = threadIdx.x; c < src.cols; c += blockDim.x) {
+      const float v = static_cast<float>(Elem<DT>::ld(src.ptr, sb + c));
+      const __nv_bfloat16 h = __float2bfloat16_rn(v);
+      hi[db + c] = h;
+      if (lo != nullptr) lo[db + c] = __float2bfloat16_rn(v - __bfloat162float(h));
+    }
+  }
+}
+
+int launch_split_bf16(const AnyMat& src, int batch, __nv_bfloat16* hi, __nv_bfloat16* lo, long long ld_dst,
+                      long long bs_dst, cudaStream_t s) {
+  if (src.rows <= 0 || src.cols <= 0 || batch <= 0) return PO_OK;
+  const int per = static_cast<int>(src.rows < 8LL * sm_count() ? src.rows : 8LL * sm_count());
+  dim3 grid(per, batch);
+  switch (src.dtype) {
+    case PO_F32: split_kernel<PO_F32><<<grid, 256, 0, s>>>(src, hi, lo, ld_dst, bs_dst); break;
+    case PO_BF16: split_kernel<PO_BF16><<<grid, 256, 0, s>>>(src, hi, lo, ld_dst, bs_dst); break;
+    case PO_F16: split_kernel<PO_F16><<<grid, 256, 0, s>>>(src, hi, lo, ld_dst, bs_dst); break;
+    case PO_F64: split_kernel<PO_F64><<<grid, 256, 0, s>>>(src, hi, lo, ld_dst, bs_dst); break;
+    default: return set_error(PO_ERR_ARG, "split: unsupported dtype");
+  }
+  return check_cuda(cudaGetLastError(), "split launch");
+}
+
+}  // namespace po

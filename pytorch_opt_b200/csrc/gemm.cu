@@ -1,0 +1,204 @@
+// Tensor-map encoding, kernel instantiation and launch of the tcgen05 GEMM,
+// plus the library-wide error plumbing.
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "gemm_launch.cuh"
+
+namespace po {
+
+// ----------------------------------------------------------- error plumbing
+static thread_local std::string g_last_error;
+
+int set_error(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return PO_OK;
+  return set_error(PO_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Written by kernels whose bounded waits gave up; read by po_device_error().
+__device__ int g_device_error = 0;
+
+static constexpr int kMaxDevices = 64;
+
+int* device_error_word() {
+  static int* ptrs[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+
+int sm_count() {
+  static int counts[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  if (counts[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    counts[dev] = n > 0 ? n : 148;
+  }
+  return counts[dev];
+}
+
+// ------------------------------------------------------------- tensor maps
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Map over a [batch][outer][inner] array, box = {box_inner, box_outer, 1},
+// 128-byte swizzle, zero fill out of bounds.
+static int encode_map(CUtensorMap* map, const MatView& v, int batch, int box_inner, int box_outer,
+                      CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return set_error(PO_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const int es = dtype_size(v.dtype);
+  if (v.dtype != PO_BF16 && v.dtype != PO_F32) return set_error(PO_ERR_ARG, "operand dtype must be bf16 or fp32");
+  if (reinterpret_cast<uintptr_t>(v.ptr) % 16 != 0 || (v.ld * es) % 16 != 0 ||
+      (batch > 1 && (v.bstride * es) % 16 != 0))
+    return set_error(PO_ERR_ARG, "tensor-core operand needs 16-byte aligned base and pitches");
+  const long long bstride_bytes = batch > 1 ? v.bstride * es : v.ld * es * (v.rows > 0 ? v.rows : 1);
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(v.cols), static_cast<cuuint64_t>(v.rows),
+                        static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(v.ld * es), static_cast<cuuint64_t>(bstride_bytes)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, v.dtype == PO_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+                  const_cast<void*>(v.ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[256];
+    snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu x %llu, ld %lld", int(r),
+             (unsigned long long)dims[0], (unsigned long long)dims[1], (unsigned long long)dims[2], v.ld);
+    return set_error(PO_ERR_CUDA, buf);
+  }
+  return PO_OK;
+}
+
+EpiIn epi_in(const void* ptr, int in_kind, long long ld, long long bstride, float beta) {
+  EpiIn e{};
+  e.ptr = ptr;
+  e.kind = in_kind;
+  e.ld = ld;
+  e.bstride = bstride;
+  e.beta = beta;
+  const int es = in_kind == IN_F32 ? 4 : 2;
+  e.vec = (reinterpret_cast<uintptr_t>(ptr) % 16 == 0) && (ld * es) % 16 == 0 && (bstride * es) % 16 == 0;
+  return e;
+}
+
+EpiOut epi_out(void* ptr, int out_kind, long long ld, long long bstride, bool trans) {
+  EpiOut e{};
+  e.ptr = ptr;
+  e.kind = out_kind;
+  e.ld = ld;
+  e.bstride = bstride;
+  e.trans = trans ? 1 : 0;
+  const int es = (out_kind == OUT_F32 || out_kind == OUT_TF32) ? 4 : (out_kind == OUT_F64 ? 8 : 2);
+  e.vec = (reinterpret_cast<uintptr_t>(ptr) % 16 == 0) && (ld * es) % 16 == 0 && (bstride * es) % 16 == 0;
+  return e;
+}
+
+int launch_gemm(const GemmDesc& d, cudaStream_t stream) {
+  if (d.M <= 0 || d.N <= 0 || d.batch <= 0) return PO_OK;
+  if (d.K <= 0) return set_error(PO_ERR_ARG, "launch_gemm: K must be positive");
+  if (d.tri && d.M != d.N) return set_error(PO_ERR_ARG, "launch_gemm: triangular product needs M == N");
+  if (d.npass != 1 && d.npass != 3) return set_error(PO_ERR_ARG, "launch_gemm: npass must be 1 or 3");
+  const int want_dtype = d.kind == KIND_BF16 ? PO_BF16 : PO_F32;
+  const int nmaps = d.npass == 3 ? 2 : 1;
+  for (int i = 0; i < nmaps; ++i)
+    if (d.a[i].dtype != want_dtype || d.b[i].dtype != want_dtype)
+      return set_error(PO_ERR_ARG, "launch_gemm: operand dtype does not match the product kind");
+  int bn = d.bn;
+  if (bn == 0) bn = (d.tri || d.N <= 128) ? 128 : 256;
+  if (d.tri || d.chunked) bn = 128;
+
+  GemmParams P;
+  memset(&P, 0, sizeof(P));
+  const int es = d.kind == KIND_BF16 ? 2 : 4;
+  const int bk = 128 / es;
+  for (int i = 0; i < 2; ++i) {
+    const int src = i < nmaps ? i : 0;
+    int r;
+    // A: logical M x K.
+    // MN-major 32-bit operands: 128 B swizzle with 32 B granules (the only
+    // shared-memory layout the tensor cores accept for MN-major tf32).
+    const CUtensorMapSwizzle mn_swz = es == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+    if (d.a_kmajor) r = encode_map(&P.mapA[i], d.a[src], d.batch, bk, 128);
+    else r = encode_map(&P.mapA[i], d.a[src], d.batch, 128 / es, bk, mn_swz);
+    if (r) return r;
+    if (d.b_kmajor) r = encode_map(&P.mapB[i], d.b[src], d.batch, bk, bn);
+    else r = encode_map(&P.mapB[i], d.b[src], d.batch, 128 / es, bk, mn_swz);
+    if (r) return r;
+  }
+  P.M = d.M;
+  P.N = d.N;
+  P.K = d.K;
+  P.batch = d.batch;
+  P.tiles_m = cdiv(d.M, 128);
+  P.tiles_n = cdiv(d.N, bn);
+  P.tri = d.tri ? 1 : 0;
+  P.tiles_per_batch = d.tri ? P.tiles_m * (P.tiles_m + 1) / 2 : P.tiles_m * P.tiles_n;
+  const long long total = static_cast<long long>(P.tiles_per_batch) * d.batch;
+  if (total > 0x7fffffffLL) return set_error(PO_ERR_ARG, "launch_gemm: too many tiles");
+  P.total_tiles = static_cast<int>(total);
+  P.npass = d.npass;
+  P.active = d.active;
+  P.passes = d.passes;
+  P.err = device_error_word();
+  if (P.err == nullptr) return set_error(PO_ERR_CUDA, "device error word unavailable");
+  P.epi = d.epi;
+
+  const bool a_mn = !d.a_kmajor, b_mn = !d.b_kmajor;
+  if (d.chunked) {
+    return d.kind == KIND_BF16 ? dispatch_major<KIND_BF16, 128, true>(P, a_mn, b_mn, stream)
+                               : dispatch_major<KIND_TF32, 128, true>(P, a_mn, b_mn, stream);
+  }
+  if (d.kind == KIND_BF16) {
+    return bn == 128 ? dispatch_major<KIND_BF16, 128, false>(P, a_mn, b_mn, stream)
+                     : dispatch_major<KIND_BF16, 256, false>(P, a_mn, b_mn, stream);
+  }
+  return bn == 128 ? dispatch_major<KIND_TF32, 128, false>(P, a_mn, b_mn, stream)
+                   : dispatch_major<KIND_TF32, 256, false>(P, a_mn, b_mn, stream);
+}
+
+}  // namespace po
+
+// ------------------------------------------------------------------ C ABI
+extern "C" const char* po_last_error(void) { return po::g_last_error.c_str(); }
+
+extern "C" int po_device_error(int reset) {
+  int* p = po::device_error_word();
+  if (p == nullptr) return -1;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  int v = 0;
+  if (cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  if (reset && v != 0) cudaMemset(p, 0, sizeof(int));
+  return v;
+}
+
+extern "C" const char* po_version(void) { return "pytorch_opt_b200 0.1 (sm_100a)"; }

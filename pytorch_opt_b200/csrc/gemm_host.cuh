@@ -1,0 +1,42 @@
+// Host-side description of one batched tensor-core product and its launcher.
+#pragma once
+
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace po {
+
+// A batched row-major matrix in device memory: [batch][rows][cols], row pitch
+// ld, batch pitch bstride (elements). dtype: PO_BF16 or PO_F32.
+struct MatView {
+  const void* ptr = nullptr;
+  int dtype = PO_BF16;
+  long long rows = 0, cols = 0, ld = 0, bstride = 0;
+};
+
+// D = epilogue(opA * opB) with opA: M x K, opB: K x N.
+//   a_kmajor: A stored as [M][K] (K contiguous); otherwise stored as [K][M].
+//   b_kmajor: B stored as [N][K] (i.e. B^T row-major); otherwise [K][N].
+struct GemmDesc {
+  int kind = KIND_BF16;  // operand format on the tensor cores
+  int M = 0, N = 0, K = 0, batch = 1;
+  MatView a[2];  // [0] plain / hi, [1] lo (npass == 3)
+  MatView b[2];
+  bool a_kmajor = true;
+  bool b_kmajor = true;
+  int npass = 1;
+  bool tri = false;
+  bool chunked = false;  // sum 256-wide K chunks in the epilogue (fp32, round to nearest); BN = 128
+  const int* active = nullptr;
+  const int* passes = nullptr;
+  int bn = 0;  // 0 = choose
+  Epilogue epi{};
+};
+
+// Helpers to fill epilogue slots.
+EpiIn epi_in(const void* ptr, int in_kind, long long ld, long long bstride, float beta);
+EpiOut epi_out(void* ptr, int out_kind, long long ld, long long bstride, bool trans = false);
+
+int launch_gemm(const GemmDesc& d, cudaStream_t stream);
+
+}  // namespace po

@@ -1,0 +1,118 @@
+// Two-sided preconditioner application out = L G R
+// (pytorch_opt/ops/reference.py:117-121; ATen version
+// pytorch_opt/ops/csrc/pytorch_opt_ops.cpp:96-99) as two chained tensor-core
+// products. The first product's epilogue writes L G directly as the operand
+// of the second (bf16 hi/lo pair for fp32 inputs, bf16 for bf16 inputs).
+#include "elementwise.cuh"
+#include "gemm_host.cuh"
+
+namespace po {
+namespace {
+
+struct PrecondBufs {
+  __nv_bfloat16 *lh, *ll, *gh, *gl, *rh, *rl, *ph, *pl;
+  long long ldl, ldg, ldr;
+};
+
+void precond_layout(Arena& ar, long long m, long long n, bool split, PrecondBufs& B) {
+  B.ldl = round_up(m, 64);
+  B.ldg = round_up(n, 64);
+  B.ldr = round_up(n, 64);
+  auto take = [&](long long elems) { return static_cast<__nv_bfloat16*>(ar.take(static_cast<size_t>(elems) * 2)); };
+  B.lh = take(m * B.ldl);
+  B.gh = take(m * B.ldg);
+  B.rh = take(n * B.ldr);
+  B.ph = take(m * B.ldg);
+  B.ll = split ? take(m * B.ldl) : nullptr;
+  B.gl = split ? take(m * B.ldg) : nullptr;
+  B.rl = split ? take(n * B.ldr) : nullptr;
+  B.pl = split ? take(m * B.ldg) : nullptr;
+}
+
+MatView bview(const __nv_bfloat16* p, long long rows, long long cols, long long ld) {
+  MatView v;
+  v.ptr = p;
+  v.dtype = PO_BF16;
+  v.rows = rows;
+  v.cols = cols;
+  v.ld = ld;
+  v.bstride = rows * ld;
+  return v;
+}
+
+}  // namespace
+}  // namespace po
+
+using namespace po;
+
+extern "C" size_t po_precond_workspace_bytes(long long m, long long n, int dtype) {
+  if (m <= 0 || n <= 0) return 0;
+  Arena ar(nullptr, 0);
+  PrecondBufs B;
+  precond_layout(ar, m, n, dtype == PO_F32, B);
+  return ar.used + 256;
+}
+
+extern "C" int po_precond_apply(const void* L, long long l_ld, const void* G, long long g_ld, const void* R,
+                                long long r_ld, void* out, long long out_ld, int dtype, long long m, long long n,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype != PO_F32 && dtype != PO_BF16) return set_error(PO_ERR_ARG, "precond_apply: dtype must be fp32 or bf16");
+  if (m < 0 || n < 0) return set_error(PO_ERR_ARG, "precond_apply: negative size");
+  if (m == 0 || n == 0) return PO_OK;
+  if (!L || !G || !R || !out) return set_error(PO_ERR_ARG, "precond_apply: null pointer");
+  if (l_ld < m || g_ld < n || r_ld < n || out_ld < n) return set_error(PO_ERR_ARG, "precond_apply: pitch too small");
+  if (m > 0x3fffffff || n > 0x3fffffff) return set_error(PO_ERR_ARG, "precond_apply: size too large");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool split = dtype == PO_F32;
+  Arena ar(workspace, workspace_bytes);
+  PrecondBufs B;
+  precond_layout(ar, m, n, split, B);
+  if (workspace == nullptr || ar.overflow()) return set_error(PO_ERR_WORKSPACE, "precond_apply: workspace too small");
+
+  int r;
+  AnyMat lm{L, dtype, m, m, l_ld, m * l_ld}, gm{G, dtype, m, n, g_ld, m * g_ld}, rm{R, dtype, n, n, r_ld, n * r_ld};
+  if ((r = launch_split_bf16(lm, 1, B.lh, B.ll, B.ldl, m * B.ldl, s))) return r;
+  if ((r = launch_split_bf16(gm, 1, B.gh, B.gl, B.ldg, m * B.ldg, s))) return r;
+  if ((r = launch_split_bf16(rm, 1, B.rh, B.rl, B.ldr, n * B.ldr, s))) return r;
+
+  // P = L G : A = L [m][m] (K-major), B = G stored [K = m][N = n] (MN-major).
+  GemmDesc g1;
+  g1.kind = KIND_BF16;
+  g1.M = static_cast<int>(m);
+  g1.N = static_cast<int>(n);
+  g1.K = static_cast<int>(m);
+  g1.a[0] = bview(B.lh, m, m, B.ldl);
+  g1.b[0] = bview(B.gh, m, n, B.ldg);
+  if (split) {
+    g1.a[1] = bview(B.ll, m, m, B.ldl);
+    g1.b[1] = bview(B.gl, m, n, B.ldg);
+    g1.npass = 3;
+  }
+  g1.b_kmajor = false;
+  g1.chunked = split && 3 * m > 2048;
+  g1.epi.alpha = 1.0f;
+  g1.epi.nout = split ? 2 : 1;
+  g1.epi.out[0] = epi_out(B.ph, OUT_BF16, B.ldg, m * B.ldg);
+  if (split) g1.epi.out[1] = epi_out(B.pl, OUT_BF16_LO, B.ldg, m * B.ldg);
+  if ((r = launch_gemm(g1, s))) return r;
+
+  // out = P R : A = P [m][n] (K-major), B = R stored [K = n][N = n] (MN-major).
+  GemmDesc g2;
+  g2.kind = KIND_BF16;
+  g2.M = static_cast<int>(m);
+  g2.N = static_cast<int>(n);
+  g2.K = static_cast<int>(n);
+  g2.a[0] = bview(B.ph, m, n, B.ldg);
+  g2.b[0] = bview(B.rh, n, n, B.ldr);
+  if (split) {
+    g2.a[1] = bview(B.pl, m, n, B.ldg);
+    g2.b[1] = bview(B.rl, n, n, B.ldr);
+    g2.npass = 3;
+  }
+  g2.b_kmajor = false;
+  g2.chunked = split && 3 * n > 2048;
+  g2.epi.alpha = 1.0f;
+  g2.epi.nout = 1;
+  g2.epi.out[0] = epi_out(out, dtype == PO_F32 ? OUT_F32 : OUT_BF16, out_ld, m * out_ld);
+  return launch_gemm(g2, s);
+}

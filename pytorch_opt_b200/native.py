@@ -1,0 +1,236 @@
+"""Native-module surface of ``pytorch_opt.ops`` on the sm_100a library.
+
+The reference's ops layer (``pytorch_opt/ops/__init__.py:58-84``) calls a
+compiled module with four positional functions, bound in
+``pytorch_opt/ops/csrc/pytorch_opt_ops.cpp:103-111``:
+
+    inverse_matrix_root(A, p, damping, method, root_f64, max_iter, tol) -> Tensor
+    newton_schulz_orthogonalize(G, steps, a, b, c, eps) -> Tensor
+    kron_factor_update_(L, R, G, beta2) -> None       (mutates L and R)
+    precond_apply_two_sided(L_root, G, R_root) -> Tensor
+
+This module exports exactly those, with the same argument meaning and the
+same error type for bad arguments (``RuntimeError``, as ``TORCH_CHECK``
+raises), implemented through the C ABI of ``libpytorch_opt_b200.so``. It is
+the object ``pytorch_opt.ops.native_build.load()`` returns once this package
+is plugged in. It serves CUDA tensors only: there is no
+CPU code path here and no silent fallback.
+
+Extra entry points used by the optimizers' hot paths:
+``kron_syrk_ema_`` (KFAC factor statistics with the EMA fused),
+``damped_inverse`` (KFAC's ``(F + gamma I)^-1`` by the Newton kernel) and
+``newton_schulz_batched`` (many matrices in few launches).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+_METHODS = ("auto", "eigh", "newton")
+_NS_DTYPES = (torch.float32, torch.bfloat16, torch.float16, torch.float64)
+
+
+def _require_cuda(*tensors: torch.Tensor) -> torch.device:
+    dev = None
+    for t in tensors:
+        if not isinstance(t, torch.Tensor):
+            raise RuntimeError(f"expected a tensor, got {type(t).__name__}")
+        if not t.is_cuda:
+            raise RuntimeError("pytorch_opt_b200 runs on CUDA tensors only (there is no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError("all tensors must be on the same CUDA device")
+    return dev
+
+
+def _call(name: str, *args) -> None:
+    lib = _lib.load()
+    _lib.check(getattr(lib, name)(*args), name)
+
+
+def _batch_view(x: torch.Tensor) -> tuple[torch.Tensor, int, int, int]:
+    """Contiguous [batch, rows, cols] view of a (..., rows, cols) tensor."""
+    rows, cols = x.shape[-2], x.shape[-1]
+    batch = math.prod(x.shape[:-2]) if x.dim() > 2 else 1
+    return x.contiguous().reshape(batch, rows, cols), batch, rows, cols
+
+
+# --------------------------------------------------------------------------
+# The four functions of the reference's native module.
+# --------------------------------------------------------------------------
+
+def newton_schulz_orthogonalize(G: torch.Tensor, steps: int, a: float, b: float, c: float,
+                                eps: float) -> torch.Tensor:
+    """Quintic Newton–Schulz polar-factor approximation (reference.py:71-97, cpp:65-81)."""
+    if not isinstance(G, torch.Tensor) or G.dim() < 2:
+        raise RuntimeError("newton_schulz_orthogonalize expects ndim >= 2")
+    dev = _require_cuda(G)
+    if G.dtype not in _NS_DTYPES:
+        raise RuntimeError(f"newton_schulz_orthogonalize: unsupported dtype {G.dtype}")
+    if int(steps) < 0:
+        raise RuntimeError("newton_schulz_orthogonalize: steps must be >= 0")
+    X, batch, rows, cols = _batch_view(G)
+    out = torch.empty_like(X)
+    if X.numel() == 0:
+        return out.reshape(G.shape)
+    with torch.cuda.device(dev):
+        lib = _lib.load()
+        nbytes = lib.po_ns_workspace_bytes(batch, rows, cols)
+        ws = _lib.workspace(nbytes, dev)
+        _call("po_newton_schulz", X.data_ptr(), _lib.DTYPE_CODE[X.dtype], batch, rows, cols, cols, rows * cols,
+              out.data_ptr(), cols, rows * cols, int(steps), float(a), float(b), float(c), float(eps), -1,
+              ws.data_ptr(), nbytes, _lib.stream_ptr(dev))
+    return out.reshape(G.shape)
+
+
+def inverse_matrix_root(A: torch.Tensor, p: int, damping: float, method: str, root_f64: bool, max_iter: int,
+                        tol: float) -> torch.Tensor:
+    """(sym(A) + damping I)^(-1/p) (reference.py:43-68, cpp:41-63).
+
+    ``method="newton"`` runs the tensor-core coupled Newton kernel.
+    ``"auto"`` and ``"eigh"`` keep the reference's eigendecomposition route
+    (``torch.linalg.eigh`` on the GPU, in fp64 when ``root_f64``).
+    """
+    if int(p) != p or int(p) < 1:
+        raise RuntimeError(f"p must be a positive integer, got {p}")
+    if method not in _METHODS:
+        raise RuntimeError(f"method must be auto|eigh|newton, got {method}")
+    if not isinstance(A, torch.Tensor) or A.dim() < 2 or A.shape[-1] != A.shape[-2]:
+        raise RuntimeError("inverse_matrix_root expects square matrices (..., d, d)")
+    dev = _require_cuda(A)
+    p = int(p)
+    if method != "newton":
+        return _eigh_root(A, p, float(damping), bool(root_f64))
+    orig = A.dtype
+    work = A if A.dtype in (torch.float32, torch.bfloat16, torch.float64) else A.float()
+    X, batch, d, _ = _batch_view(work)
+    out = torch.empty_like(X)
+    if X.numel() == 0:
+        return out.reshape(A.shape).to(orig)
+    with torch.cuda.device(dev):
+        lib = _lib.load()
+        nbytes = lib.po_root_workspace_bytes(batch, d, p)
+        ws = _lib.workspace(nbytes, dev)
+        _call("po_inverse_root", X.data_ptr(), _lib.DTYPE_CODE[X.dtype], batch, d, d, d * d, out.data_ptr(), d,
+              d * d, p, float(damping), int(max_iter), float(tol), None, ws.data_ptr(), nbytes, _lib.stream_ptr(dev))
+    return out.reshape(A.shape).to(orig)
+
+
+def kron_factor_update_(L: torch.Tensor, R: torch.Tensor, G: torch.Tensor, beta2: float) -> None:
+    """In place: L <- b L + (1-b) G G^T, R <- b R + (1-b) G^T G (reference.py:100-114, cpp:83-94)."""
+    if not isinstance(G, torch.Tensor) or G.dim() != 2:
+        raise RuntimeError("G must be 2D")
+    dev = _require_cuda(L, R, G)
+    m, n = G.shape
+    if tuple(L.shape) != (m, m) or tuple(R.shape) != (n, n):
+        raise RuntimeError(f"factor shapes {tuple(L.shape)}, {tuple(R.shape)} do not match G {tuple(G.shape)}")
+    Lw = L if (L.dtype == torch.float32 and L.is_contiguous()) else L.float().contiguous()
+    Rw = R if (R.dtype == torch.float32 and R.is_contiguous()) else R.float().contiguous()
+    Gw = G if G.dtype in (torch.float32, torch.bfloat16) else G.float()
+    Gw = Gw.contiguous()
+    if m and n:
+        with torch.cuda.device(dev):
+            lib = _lib.load()
+            code = _lib.DTYPE_CODE[Gw.dtype]
+            nbytes = lib.po_kron_workspace_bytes(m, n, code)
+            ws = _lib.workspace(nbytes, dev)
+            _call("po_kron_factor_update", Lw.data_ptr(), m, Rw.data_ptr(), n, Gw.data_ptr(), code, m, n, n,
+                  float(beta2), ws.data_ptr(), nbytes, _lib.stream_ptr(dev))
+    if Lw is not L:
+        L.copy_(Lw)
+    if Rw is not R:
+        R.copy_(Rw)
+
+
+def precond_apply_two_sided(L_root: torch.Tensor, G: torch.Tensor, R_root: torch.Tensor) -> torch.Tensor:
+    """L_root @ G @ R_root (reference.py:117-121, cpp:96-99)."""
+    dev = _require_cuda(L_root, G, R_root)
+    if G.dim() != 2 or L_root.dim() != 2 or R_root.dim() != 2:
+        raise RuntimeError("precond_apply_two_sided expects 2D operands")
+    m, n = G.shape
+    if tuple(L_root.shape) != (m, m) or tuple(R_root.shape) != (n, n):
+        raise RuntimeError("precond_apply_two_sided: shape mismatch")
+    dt = G.dtype if G.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    Lc, Gc, Rc = (t.to(dt).contiguous() for t in (L_root, G, R_root))
+    out = torch.empty(m, n, dtype=dt, device=dev)
+    if m and n:
+        with torch.cuda.device(dev):
+            lib = _lib.load()
+            code = _lib.DTYPE_CODE[dt]
+            nbytes = lib.po_precond_workspace_bytes(m, n, code)
+            ws = _lib.workspace(nbytes, dev)
+            _call("po_precond_apply", Lc.data_ptr(), m, Gc.data_ptr(), n, Rc.data_ptr(), n, out.data_ptr(), n, code,
+                  m, n, ws.data_ptr(), nbytes, _lib.stream_ptr(dev))
+    return out if out.dtype == G.dtype else out.to(G.dtype)
+
+
+# --------------------------------------------------------------------------
+# Extra hot-path entry points.
+# --------------------------------------------------------------------------
+
+def kron_syrk_ema_(F: torch.Tensor, X: torch.Tensor, alpha: float, beta: float, first: bool) -> torch.Tensor:
+    """In place: F <- alpha X^T X when ``first`` else beta F + (1 - beta) alpha X^T X.
+
+    The KFAC factor statistic of ``pytorch_opt/curvature/kron.py:105-113``
+    (A = a^T a / n: alpha = 1/n; G = ghat^T ghat / n with ghat = n g:
+    alpha = n, applied to g) with the EMA of ``kron.py:95-103``.
+    """
+    dev = _require_cuda(F, X)
+    if X.dim() != 2 or F.dim() != 2 or F.shape[0] != F.shape[1] or F.shape[0] != X.shape[1]:
+        raise RuntimeError("kron_syrk_ema_: expects X (rows, d) and F (d, d)")
+    if F.dtype != torch.float32 or not F.is_contiguous():
+        raise RuntimeError("kron_syrk_ema_: F must be a contiguous fp32 tensor")
+    Xw = (X if X.dtype in (torch.float32, torch.bfloat16) else X.float()).contiguous()
+    rows, d = Xw.shape
+    with torch.cuda.device(dev):
+        lib = _lib.load()
+        code = _lib.DTYPE_CODE[Xw.dtype]
+        nbytes = lib.po_syrk_workspace_bytes(rows, d, code)
+        ws = _lib.workspace(nbytes, dev)
+        _call("po_syrk_ema", F.data_ptr(), d, d, Xw.data_ptr(), code, rows, d, float(alpha), float(beta),
+              1 if first else 0, ws.data_ptr(), nbytes, _lib.stream_ptr(dev))
+    return F
+
+
+def damped_inverse(F: torch.Tensor, gamma: float, max_iter: int = 100, tol: float = 1e-10) -> torch.Tensor:
+    """(sym(F) + gamma I)^-1 by the coupled Newton kernel with p = 1.
+
+    Tensor-core replacement for the fp64 ``eigh`` inverse of
+    ``pytorch_opt/optim/kfac.py:134-138``.
+    """
+    return inverse_matrix_root(F, 1, gamma, "newton", True, max_iter, tol)
+
+
+def newton_schulz_batched(Gs, steps: int = 5, coeffs=(3.4445, -4.7750, 2.0315), eps: float = 1e-7):
+    """Orthogonalise many matrices: a 3-D tensor, or a list grouped by (shape, dtype) into batched launches."""
+    a, b, c = coeffs
+    if isinstance(Gs, torch.Tensor):
+        return newton_schulz_orthogonalize(Gs, steps, a, b, c, eps)
+    groups: dict = {}
+    for i, g in enumerate(Gs):
+        groups.setdefault((tuple(g.shape), g.dtype, g.device), []).append(i)
+    out = [None] * len(Gs)
+    for (_, _, _), idx in groups.items():
+        stacked = torch.stack([Gs[i] for i in idx])
+        res = newton_schulz_orthogonalize(stacked, steps, a, b, c, eps)
+        for j, i in enumerate(idx):
+            out[i] = res[j]
+    return out
+
+
+def _eigh_root(A: torch.Tensor, p: int, damping: float, root_f64: bool) -> torch.Tensor:
+    orig = A.dtype
+    work = torch.float64 if root_f64 else torch.float32
+    M = A.to(work)
+    M = 0.5 * (M + M.mT)
+    if damping:
+        M = M + damping * torch.eye(M.shape[-1], dtype=work, device=M.device).expand_as(M)
+    evals, evecs = torch.linalg.eigh(M)
+    evals = evals.clamp_min(1e-30)
+    root = evecs @ torch.diag_embed(evals.pow(-1.0 / p)) @ evecs.mT
+    return (0.5 * (root + root.mT)).to(orig)
