@@ -59,8 +59,10 @@ const char* po_version(void);
  * input dtype. G and out: [batch][rows][cols] of `dtype`
  * (PO_F32 / PO_BF16 / PO_F16 / PO_F64). The first (steps - tf32_tail)
  * iterations run bf16 tensor-core products, the last `tf32_tail` run tf32
- * products, all accumulating in fp32. tf32_tail < 0 selects the default:
- * 2 when min(rows, cols) >= 512, else all steps.
+ * products, all accumulating in fp32. tf32_tail < 0 selects the default
+ * schedule by m = min(rows, cols): m >= 512: two tf32 steps after bf16 ones;
+ * 256 <= m < 512: tf32 on every step; m < 256: split-bf16 pairs
+ * (hi*hi + hi*lo + lo*hi) on every step.
  * ---------------------------------------------------------------------- */
 size_t po_ns_workspace_bytes(long long batch, long long rows, long long cols);
 int po_newton_schulz(const void* G, int dtype, long long batch, long long rows, long long cols, long long ld,

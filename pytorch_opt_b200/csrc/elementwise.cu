@@ -83,8 +83,8 @@ int launch_sumsq(const AnyMat& M, int batch, double* sums, cudaStream_t s) {
 // One 32x32 output tile per block (32 x 8 threads). Output element (r, c)
 // comes from src(c, r) when TRANS.
 template <int DT, bool TRANS>
-__global__ void ns_pack_kernel(AnyMat src, const double* sums, float eps, float* xf, void* xop, int op_kind,
-                               long long ldx, long long rows_out, long long cols_out) {
+__global__ void ns_pack_kernel(AnyMat src, const double* sums, float eps, float* xf, void* xop, void* xlo,
+                               int op_kind, long long ldx, long long rows_out, long long cols_out) {
   __shared__ float tile[32][33];
   const int b = blockIdx.z;
   const long long r0 = static_cast<long long>(blockIdx.y) * 32, c0 = static_cast<long long>(blockIdx.x) * 32;
@@ -108,27 +108,34 @@ __global__ void ns_pack_kernel(AnyMat src, const double* sums, float eps, float*
     v = __fdiv_rn(v, den);
     const long long o = xbase + r * ldx + c;
     xf[o] = v;
-    if (op_kind == OUT_BF16) static_cast<__nv_bfloat16*>(xop)[o] = __float2bfloat16_rn(v);
-    else static_cast<float*>(xop)[o] = round_tf32(v);
+    if (op_kind == OUT_BF16) {
+      const __nv_bfloat16 h = __float2bfloat16_rn(v);
+      static_cast<__nv_bfloat16*>(xop)[o] = h;
+      if (xlo != nullptr) static_cast<__nv_bfloat16*>(xlo)[o] = __float2bfloat16_rn(v - __bfloat162float(h));
+    } else {
+      static_cast<float*>(xop)[o] = round_tf32(v);
+    }
   }
 }
 
 template <int DT>
 static void ns_pack_dt(const AnyMat& src, int batch, bool trans, const double* sums, float eps, float* xf, void* xop,
-                       int op_kind, long long ldx, long long rows_out, long long cols_out, cudaStream_t s) {
+                       void* xlo, int op_kind, long long ldx, long long rows_out, long long cols_out, cudaStream_t s) {
   dim3 grid(cdiv(cols_out, 32), cdiv(rows_out, 32), batch), block(32, 8);
-  if (trans) ns_pack_kernel<DT, true><<<grid, block, 0, s>>>(src, sums, eps, xf, xop, op_kind, ldx, rows_out, cols_out);
-  else ns_pack_kernel<DT, false><<<grid, block, 0, s>>>(src, sums, eps, xf, xop, op_kind, ldx, rows_out, cols_out);
+  if (trans)
+    ns_pack_kernel<DT, true><<<grid, block, 0, s>>>(src, sums, eps, xf, xop, xlo, op_kind, ldx, rows_out, cols_out);
+  else
+    ns_pack_kernel<DT, false><<<grid, block, 0, s>>>(src, sums, eps, xf, xop, xlo, op_kind, ldx, rows_out, cols_out);
 }
 
 int launch_ns_pack(const AnyMat& src, int batch, bool trans, const double* sums, float eps, float* xf, void* xop,
-                   int op_kind, long long ldx, long long rows_out, long long cols_out, cudaStream_t s) {
+                   void* xlo, int op_kind, long long ldx, long long rows_out, long long cols_out, cudaStream_t s) {
   if (rows_out <= 0 || cols_out <= 0 || batch <= 0) return PO_OK;
   switch (src.dtype) {
-    case PO_F32: ns_pack_dt<PO_F32>(src, batch, trans, sums, eps, xf, xop, op_kind, ldx, rows_out, cols_out, s); break;
-    case PO_BF16: ns_pack_dt<PO_BF16>(src, batch, trans, sums, eps, xf, xop, op_kind, ldx, rows_out, cols_out, s); break;
-    case PO_F16: ns_pack_dt<PO_F16>(src, batch, trans, sums, eps, xf, xop, op_kind, ldx, rows_out, cols_out, s); break;
-    case PO_F64: ns_pack_dt<PO_F64>(src, batch, trans, sums, eps, xf, xop, op_kind, ldx, rows_out, cols_out, s); break;
+    case PO_F32: ns_pack_dt<PO_F32>(src, batch, trans, sums, eps, xf, xop, xlo, op_kind, ldx, rows_out, cols_out, s); break;
+    case PO_BF16: ns_pack_dt<PO_BF16>(src, batch, trans, sums, eps, xf, xop, xlo, op_kind, ldx, rows_out, cols_out, s); break;
+    case PO_F16: ns_pack_dt<PO_F16>(src, batch, trans, sums, eps, xf, xop, xlo, op_kind, ldx, rows_out, cols_out, s); break;
+    case PO_F64: ns_pack_dt<PO_F64>(src, batch, trans, sums, eps, xf, xop, xlo, op_kind, ldx, rows_out, cols_out, s); break;
     default: return set_error(PO_ERR_ARG, "ns_pack: unsupported dtype");
   }
   return check_cuda(cudaGetLastError(), "ns_pack launch");

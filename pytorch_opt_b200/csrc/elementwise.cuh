@@ -22,10 +22,12 @@ int launch_sumsq(const AnyMat& M, int batch, double* sums, cudaStream_t s);
 // Pack a matrix batch into the Newton–Schulz working buffers:
 //   X[b] = src[b] (transposed when `trans`) / (sqrt(sums[b]) + eps)
 // written as fp32 master (xf, pitch ldx) and as the first product operand
-// (xop: bf16 when op_kind == OUT_BF16, tf32-rounded fp32 when OUT_TF32).
+// (xop: bf16 when op_kind == OUT_BF16, tf32-rounded fp32 when OUT_TF32;
+// with OUT_BF16 and a non-null xlo, also the low bf16 half of a split pair).
 // The packed matrix is rows_out x cols_out.
 int launch_ns_pack(const AnyMat& src, int batch, bool trans, const double* sums, float eps, float* xf,
-                   void* xop, int op_kind, long long ldx, long long rows_out, long long cols_out, cudaStream_t s);
+                   void* xop, void* xlo, int op_kind, long long ldx, long long rows_out, long long cols_out,
+                   cudaStream_t s);
 
 // out[b] = cast(src[b]) (transposed when `trans`); src fp32 [rows][cols].
 int launch_copy_out(const float* src, long long ld_src, long long bs_src, int batch, long long rows, long long cols,

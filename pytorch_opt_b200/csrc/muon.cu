@@ -33,13 +33,15 @@ __device__ __forceinline__ float round_to(float v) {
 template <typename T>
 __global__ void momentum_kernel(const T* __restrict__ g, T* __restrict__ buf, T* __restrict__ u, long long n,
                                 float mu, int nesterov) {
+  // torch's add(..., alpha) on a bf16 tensor rounds alpha to bf16 first; mul_ by a scalar does not.
+  const float mu_alpha = round_to<T>(mu);
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const float gi = ld(g, i);
     const float b1 = round_to<T>(ld(buf, i) * mu);  // buf.mul_(mu)
     const float b2 = round_to<T>(b1 + gi);          // buf.add_(g)
     buf[i] = cvt<T>(b2);
-    u[i] = nesterov ? cvt<T>(gi + mu * b2) : cvt<T>(b2);  // g.add(buf, alpha=mu)
+    u[i] = nesterov ? cvt<T>(gi + mu_alpha * b2) : cvt<T>(b2);  // g.add(buf, alpha=mu)
   }
 }
 
@@ -53,12 +55,13 @@ template <typename T>
 __global__ void apply_kernel(T* __restrict__ p, const T* __restrict__ o, long long n, float neg_eff, float decay,
                              int use_decay, double* sq) {
   double acc = 0.0;
+  const float alpha = round_to<T>(neg_eff);  // add_(o, alpha=-eff) rounds alpha to the tensor dtype
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     float pi = ld(p, i);
     if (use_decay) pi = round_to<T>(pi * decay);  // p.mul_(1 - lr * wd)
     const float oi = ld(o, i);
-    p[i] = cvt<T>(fmaf(neg_eff, oi, pi));  // p.add_(upd, alpha=-eff)
+    p[i] = cvt<T>(fmaf(alpha, oi, pi));  // p.add_(upd, alpha=-eff)
     acc += static_cast<double>(oi) * oi;
   }
   if (sq != nullptr) {

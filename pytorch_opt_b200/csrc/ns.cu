@@ -8,8 +8,11 @@
 //            X = a X + B X      (fp32 master copy of X updated in place)
 //   the last update writes the caller's output directly (transposed back,
 //   cast to the input dtype).
-// Iterations before the last `tf32_tail` ones use bf16 operands, the tail
-// uses tf32 operands rounded to nearest; all products accumulate in fp32.
+// Precision per step: bf16 operands on all but the last `tf32_tail` steps,
+// tf32 operands (rounded to nearest) on the tail; matrices with m < 256 run
+// every step on split-bf16 pairs (hi*hi + hi*lo + lo*hi) with chunked
+// accumulation instead, which keeps even long or oscillating schedules close
+// to the fp32 reference. All products accumulate in fp32.
 #include "elementwise.cuh"
 #include "gemm_host.cuh"
 
@@ -17,36 +20,40 @@ namespace po {
 
 namespace {
 
+enum Prec : int { P_BF16 = 0, P_TF32 = 1, P_SPLIT = 2 };
+
+// m below which the automatic schedule uses split-bf16 on every step.
+constexpr long long kSplitBelow = 256;
+// m below which the automatic schedule uses tf32 on every step.
+constexpr long long kTf32Below = 512;
+
 struct NsBuffers {
   float* xf;                // fp32 master X            [batch][m][ldx]
-  __nv_bfloat16* xb[2];     // bf16 operand copies of X (ping-pong)
+  __nv_bfloat16* xb[2];     // bf16 (hi) operand copies of X (ping-pong)
+  __nv_bfloat16* xl[2];     // bf16 lo halves for split steps (allocated only when used)
   float* xt[2];             // tf32-rounded operand copies of X (ping-pong)
   float* af;                // fp32 A = X X^T           [batch][m][ldm]
-  void* aop;                // A as product operand (bf16 or tf32)
-  void* bop;                // B as product operand (bf16 or tf32)
+  char* aop;                // A as product operand: fp32 (tf32) or bf16 hi | bf16 lo
+  char* bop;                // B as product operand, same layout
   double* sums;             // per-matrix sum of squares
-  long long ldx, ldm;
+  long long ldx, ldm, msz;  // msz: elements of one [batch][m][ldm] array
 };
 
-void ns_layout(Arena& ar, long long batch, long long m, long long n, NsBuffers& B) {
+void ns_layout(Arena& ar, long long batch, long long m, long long n, bool split, NsBuffers& B) {
   B.ldx = round_up(n, 64);
   B.ldm = round_up(m, 64);
   const size_t xs = static_cast<size_t>(batch * m * B.ldx);
-  const size_t ms = static_cast<size_t>(batch * m * B.ldm);
+  B.msz = batch * m * B.ldm;
+  const size_t ms = static_cast<size_t>(B.msz);
   B.xf = static_cast<float*>(ar.take(xs * 4));
   for (int i = 0; i < 2; ++i) B.xb[i] = static_cast<__nv_bfloat16*>(ar.take(xs * 2));
+  for (int i = 0; i < 2; ++i) B.xl[i] = split ? static_cast<__nv_bfloat16*>(ar.take(xs * 2)) : nullptr;
   for (int i = 0; i < 2; ++i) B.xt[i] = static_cast<float*>(ar.take(xs * 4));
   B.af = static_cast<float*>(ar.take(ms * 4));
-  B.aop = ar.take(ms * 4);
-  B.bop = ar.take(ms * 4);
+  B.aop = static_cast<char*>(ar.take(ms * 4));
+  B.bop = static_cast<char*>(ar.take(ms * 4));
   B.sums = static_cast<double*>(ar.take(static_cast<size_t>(batch) * 8));
 }
-
-// Default precision schedule. bf16 products on all but the last two steps
-// keep the result within 1e-2 (relative Frobenius) of the fp32 reference for
-// m >= 512; smaller matrices, whose error is dominated by fewer singular
-// values, run every step on tf32 (they are cheap).
-int ns_auto_tf32_tail(long long m, int steps) { return m < 512 ? steps : (steps < 2 ? steps : 2); }
 
 int out_kind_of(int dtype) {
   switch (dtype) {
@@ -68,6 +75,38 @@ MatView view(const void* p, int dtype, long long rows, long long cols, long long
   return v;
 }
 
+// Operand views (hi, lo) of a product operand stored with precision `pr`.
+struct OpView {
+  MatView v[2];
+};
+OpView op_view(Prec pr, const void* hi, const void* lo, long long rows, long long cols, long long ld) {
+  OpView o;
+  if (pr == P_TF32) {
+    o.v[0] = view(hi, PO_F32, rows, cols, ld);
+    o.v[1] = o.v[0];
+  } else {
+    o.v[0] = view(hi, PO_BF16, rows, cols, ld);
+    o.v[1] = pr == P_SPLIT ? view(lo, PO_BF16, rows, cols, ld) : o.v[0];
+  }
+  return o;
+}
+
+// Append the epilogue outputs that write an operand of precision `pr`.
+void add_op_outputs(Epilogue& e, Prec pr, void* hi, void* lo, long long ld, long long bs) {
+  if (pr == P_TF32) {
+    e.out[e.nout++] = epi_out(hi, OUT_TF32, ld, bs);
+  } else {
+    e.out[e.nout++] = epi_out(hi, OUT_BF16, ld, bs);
+    if (pr == P_SPLIT) e.out[e.nout++] = epi_out(lo, OUT_BF16_LO, ld, bs);
+  }
+}
+
+void set_kind(GemmDesc& g, Prec pr) {
+  g.kind = pr == P_TF32 ? KIND_TF32 : KIND_BF16;
+  g.npass = pr == P_SPLIT ? 3 : 1;
+  g.chunked = pr == P_SPLIT;
+}
+
 }  // namespace
 
 }  // namespace po
@@ -79,7 +118,7 @@ extern "C" size_t po_ns_workspace_bytes(long long batch, long long rows, long lo
   const long long m = rows < cols ? rows : cols, n = rows < cols ? cols : rows;
   Arena ar(nullptr, 0);
   NsBuffers B;
-  ns_layout(ar, batch, m, n, B);
+  ns_layout(ar, batch, m, n, m < kSplitBelow, B);
   return ar.used + 256;
 }
 
@@ -95,16 +134,23 @@ extern "C" int po_newton_schulz(const void* G, int dtype, long long batch, long 
   if (G == nullptr || out == nullptr) return set_error(PO_ERR_ARG, "newton_schulz: null pointer");
   if (ld < cols || out_ld < cols) return set_error(PO_ERR_ARG, "newton_schulz: row pitch smaller than cols");
   if (batch > 65535) return set_error(PO_ERR_ARG, "newton_schulz: batch too large (max 65535)");
-  if (tf32_tail < 0) tf32_tail = ns_auto_tf32_tail(rows < cols ? rows : cols, steps);
-  if (tf32_tail > steps) tf32_tail = steps;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
   const bool trans = rows > cols;
   const long long m = trans ? cols : rows, n = trans ? rows : cols;
   if (m > 0x7fffffffLL / 2 || n > 0x7fffffffLL / 2) return set_error(PO_ERR_ARG, "newton_schulz: matrix too large");
+  // Precision schedule.
+  const bool split = tf32_tail < 0 && m < kSplitBelow;
+  if (tf32_tail < 0) tf32_tail = m < kTf32Below ? steps : (steps < 2 ? steps : 2);
+  if (tf32_tail > steps) tf32_tail = steps;
+  auto prec_of = [&](int it) -> Prec {
+    if (split) return P_SPLIT;
+    return it >= steps - tf32_tail ? P_TF32 : P_BF16;
+  };
+
   Arena ar(workspace, workspace_bytes);
   NsBuffers B;
-  ns_layout(ar, batch, m, n, B);
+  ns_layout(ar, batch, m, n, split, B);
   if (workspace == nullptr || ar.overflow())
     return set_error(PO_ERR_WORKSPACE, "newton_schulz: workspace too small (query po_ns_workspace_bytes)");
 
@@ -112,78 +158,79 @@ extern "C" int po_newton_schulz(const void* G, int dtype, long long batch, long 
   if (r) return r;
   AnyMat src{G, dtype, rows, cols, ld, bstride};
   if ((r = launch_sumsq(src, static_cast<int>(batch), B.sums, s))) return r;
-  const bool first_tf32 = steps - tf32_tail <= 0;
+  const Prec p0 = prec_of(0);
   if ((r = launch_ns_pack(src, static_cast<int>(batch), trans, B.sums, eps, B.xf,
-                          first_tf32 ? static_cast<void*>(B.xt[0]) : static_cast<void*>(B.xb[0]),
-                          first_tf32 ? OUT_TF32 : OUT_BF16, B.ldx, m, n, s)))
+                          p0 == P_TF32 ? static_cast<void*>(B.xt[0]) : static_cast<void*>(B.xb[0]),
+                          p0 == P_SPLIT ? static_cast<void*>(B.xl[0]) : nullptr, p0 == P_TF32 ? OUT_TF32 : OUT_BF16,
+                          B.ldx, m, n, s)))
     return r;
   if (steps == 0)
     return launch_copy_out(B.xf, B.ldx, m * B.ldx, static_cast<int>(batch), m, n, trans, out, dtype, out_ld,
                            out_bstride, s);
 
   const long long xs = m * B.ldx, ms = m * B.ldm;
+  // Operand arrays of A and B: fp32 for tf32 steps, else bf16 hi then bf16 lo.
+  char* a_hi = B.aop;
+  char* a_lo = B.aop + B.msz * 2;
+  char* b_hi = B.bop;
+  char* b_lo = B.bop + B.msz * 2;
   int cur = 0;
   for (int it = 0; it < steps; ++it) {
-    const bool tf = it >= steps - tf32_tail;
-    const int kind = tf ? KIND_TF32 : KIND_BF16;
-    const int op_dt = tf ? PO_F32 : PO_BF16;
-    const int op_out = tf ? OUT_TF32 : OUT_BF16;
-    const MatView X = tf ? view(B.xt[cur], PO_F32, m, n, B.ldx) : view(B.xb[cur], PO_BF16, m, n, B.ldx);
-    const MatView Aop = view(B.aop, op_dt, m, m, B.ldm);
-    const MatView Bop = view(B.bop, op_dt, m, m, B.ldm);
+    const Prec pr = prec_of(it);
+    const OpView X = pr == P_TF32 ? op_view(pr, B.xt[cur], nullptr, m, n, B.ldx)
+                                  : op_view(pr, B.xb[cur], B.xl[cur], m, n, B.ldx);
+    const OpView Aop = op_view(pr, a_hi, a_lo, m, m, B.ldm);
+    const OpView Bop = op_view(pr, b_hi, b_lo, m, m, B.ldm);
 
     // A = X X^T
     GemmDesc g;
-    g.kind = kind;
+    set_kind(g, pr);
     g.M = g.N = static_cast<int>(m);
     g.K = static_cast<int>(n);
     g.batch = static_cast<int>(batch);
-    g.a[0] = X;
-    g.b[0] = X;
+    g.a[0] = X.v[0]; g.a[1] = X.v[1];
+    g.b[0] = X.v[0]; g.b[1] = X.v[1];
     g.tri = true;
     g.epi.alpha = 1.0f;
-    g.epi.nout = 2;
-    g.epi.out[0] = epi_out(B.af, OUT_F32, B.ldm, ms);
-    g.epi.out[1] = epi_out(B.aop, op_out, B.ldm, ms);
+    g.epi.out[g.epi.nout++] = epi_out(B.af, OUT_F32, B.ldm, ms);
+    add_op_outputs(g.epi, pr, a_hi, a_lo, B.ldm, ms);
     if ((r = launch_gemm(g, s))) return r;
 
     // B = b A + c A A
     GemmDesc q;
-    q.kind = kind;
+    set_kind(q, pr);
     q.M = q.N = q.K = static_cast<int>(m);
     q.batch = static_cast<int>(batch);
-    q.a[0] = Aop;
-    q.b[0] = Aop;
+    q.a[0] = Aop.v[0]; q.a[1] = Aop.v[1];
+    q.b[0] = Aop.v[0]; q.b[1] = Aop.v[1];
     q.tri = true;
     q.epi.alpha = c;
     q.epi.nin = 1;
     q.epi.in[0] = epi_in(B.af, IN_F32, B.ldm, ms, b);
-    q.epi.nout = 1;
-    q.epi.out[0] = epi_out(B.bop, op_out, B.ldm, ms);
+    add_op_outputs(q.epi, pr, b_hi, b_lo, B.ldm, ms);
     if ((r = launch_gemm(q, s))) return r;
 
     // X = a X + B X ; B operand is X stored [K = m][N = n] (MN-major).
     GemmDesc u;
-    u.kind = kind;
+    set_kind(u, pr);
     u.M = static_cast<int>(m);
     u.N = static_cast<int>(n);
     u.K = static_cast<int>(m);
     u.batch = static_cast<int>(batch);
-    u.a[0] = Bop;
-    u.b[0] = X;
+    u.a[0] = Bop.v[0]; u.a[1] = Bop.v[1];
+    u.b[0] = X.v[0]; u.b[1] = X.v[1];
     u.b_kmajor = false;
     u.epi.alpha = 1.0f;
     u.epi.nin = 1;
     u.epi.in[0] = epi_in(B.xf, IN_F32, B.ldx, xs, a);
     if (it + 1 < steps) {
-      const bool next_tf = it + 1 >= steps - tf32_tail;
+      const Prec pn = prec_of(it + 1);
       const int nxt = cur ^ 1;
-      u.epi.nout = 2;
-      u.epi.out[0] = epi_out(B.xf, OUT_F32, B.ldx, xs);
-      u.epi.out[1] = next_tf ? epi_out(B.xt[nxt], OUT_TF32, B.ldx, xs) : epi_out(B.xb[nxt], OUT_BF16, B.ldx, xs);
+      u.epi.out[u.epi.nout++] = epi_out(B.xf, OUT_F32, B.ldx, xs);
+      if (pn == P_TF32) add_op_outputs(u.epi, pn, B.xt[nxt], nullptr, B.ldx, xs);
+      else add_op_outputs(u.epi, pn, B.xb[nxt], B.xl[nxt], B.ldx, xs);
     } else {
-      u.epi.nout = 1;
-      u.epi.out[0] = epi_out(out, out_kind_of(dtype), out_ld, out_bstride, trans);
+      u.epi.out[u.epi.nout++] = epi_out(out, out_kind_of(dtype), out_ld, out_bstride, trans);
     }
     if ((r = launch_gemm(u, s))) return r;
     cur ^= 1;

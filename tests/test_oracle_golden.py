@@ -1,0 +1,121 @@
+"""The numpy oracle against golden vectors produced by the reference itself.
+
+``tests/golden/*.npz`` were written by ``tests/golden/make_golden.py`` from
+kavinravi/pytorch-opt's own ``ops.reference``, ``KronTracker``,
+``kfac_factored_damping``, ``KFAC._damped_inverse`` and ``Muon`` on seeded
+inputs. Passing here pins ``oracle/ops_np.py`` before it is trusted as the
+checker of the GPU kernels.
+"""
+
+import os
+
+import numpy as np
+import pytest
+
+from oracle import ops_np as O
+from tests.conftest import GOLDEN_DIR
+
+
+def _load(name):
+    return np.load(os.path.join(GOLDEN_DIR, name))
+
+
+def _rel(a, b):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
+
+
+def test_newton_schulz_golden():
+    z = _load("ns.npz")
+    for i in range(int(z["ncases"])):
+        x, want, (steps, dt) = z[f"case{i}_in"], z[f"case{i}_out"], z[f"case{i}_meta"]
+        got = O.newton_schulz(x, int(steps), out_bf16=(dt == 1))
+        tol = {0: 1e-5, 1: 2e-3, 3: 1e-12}[int(dt)]
+        assert _rel(got, want) < tol, (i, _rel(got, want))
+
+
+def test_inverse_root_golden():
+    z = _load("roots.npz")
+    for i in range(int(z["ncases"])):
+        A, want, (p, damping, m) = z[f"case{i}_in"], z[f"case{i}_out"], z[f"case{i}_meta"]
+        method = ("auto", "eigh", "newton")[int(m)]
+        got = O.inverse_matrix_root(A, int(p), damping=float(damping), method=method)
+        tol = 1e-10 if A.dtype == np.float64 else 1e-6
+        assert got.dtype == A.dtype
+        assert _rel(got, want) < tol, (i, method, _rel(got, want))
+
+
+def test_inverse_root_argument_errors():
+    A = np.eye(3)
+    with pytest.raises(ValueError, match="positive integer"):
+        O.inverse_matrix_root(A, 0)
+    with pytest.raises(ValueError, match="method"):
+        O.inverse_matrix_root(A, 2, method="qr")
+
+
+def test_kron_factor_update_golden():
+    z = _load("kron.npz")
+    for i in range(int(z["ncases"])):
+        G1, G2 = z[f"case{i}_G1"], z[f"case{i}_G2"]
+        m, n = G1.shape
+        for beta in (1.0, 0.9):
+            L, R = np.zeros((m, m), np.float32), np.zeros((n, n), np.float32)
+            L, R = O.kron_factor_update(L, R, G1, beta)
+            L, R = O.kron_factor_update(L, R, G2, beta)
+            assert _rel(L, z[f"case{i}_L_{beta}"]) < 1e-6
+            assert _rel(R, z[f"case{i}_R_{beta}"]) < 1e-6
+    with pytest.raises(ValueError, match="2D"):
+        O.kron_factor_update(np.zeros((2, 2)), np.zeros((2, 2)), np.zeros((2, 2, 2)))
+
+
+def test_precond_golden():
+    z = _load("precond.npz")
+    for i in range(int(z["ncases"])):
+        got = O.precond_apply(z[f"case{i}_L"], z[f"case{i}_G"], z[f"case{i}_R"])
+        assert _rel(got, z[f"case{i}_out"]) < 1e-6
+
+
+def test_kfac_factors_damping_inverse_golden():
+    z = _load("kfac.npz")
+    for i in range(int(z["ncases"])):
+        bias, ema = z[f"case{i}_meta"]
+        ema = None if ema < 0 else float(ema)
+        A = G = None
+        for step in range(3):
+            Ab, Gb = O.kfac_batch_factors_linear(z[f"case{i}_a{step}"], z[f"case{i}_g{step}"], bool(bias))
+            A = O.kfac_update(A, Ab, ema, step)
+            G = O.kfac_update(G, Gb, ema, step)
+        assert _rel(A, z[f"case{i}_A"]) < 1e-6
+        assert _rel(G, z[f"case{i}_G"]) < 1e-6
+        ga, gg = O.kfac_factored_damping(z[f"case{i}_A"], z[f"case{i}_G"], 1e-3)
+        np.testing.assert_allclose([ga, gg], z[f"case{i}_gammas"], rtol=1e-6)  # fp32 traces
+        iA, cA = O.kfac_damped_inverse(z[f"case{i}_A"], ga)
+        iG, cG = O.kfac_damped_inverse(z[f"case{i}_G"], gg)
+        assert _rel(iA, z[f"case{i}_iA"]) < 1e-6 and _rel(iG, z[f"case{i}_iG"]) < 1e-6
+        np.testing.assert_allclose([cA, cG], z[f"case{i}_conds"], rtol=1e-6)
+
+
+def test_muon_golden():
+    z = _load("muon.npz")
+    lr, mom, nest, steps, wd = z["hparams"]
+    for k in range(int(z["nparams"])):
+        p, buf = z[f"p{k}_init"], np.zeros_like(z[f"p{k}_init"])
+        for s in range(2):
+            p, buf, _, _ = O.muon_matrix_step(p, z[f"p{k}_grad{s}"], buf, lr=float(lr), momentum=float(mom),
+                                              nesterov=bool(nest), ns_steps=int(steps), weight_decay=float(wd))
+        # Momentum never passes through a matrix product: bit-exact.
+        np.testing.assert_array_equal(buf, z[f"p{k}_buf"])
+        # The update goes through fp32 products whose summation order differs
+        # from torch's; after bf16 rounding a few elements may differ by an ulp.
+        dp_got, dp_want = p - z[f"p{k}_init"], z[f"p{k}_final"] - z[f"p{k}_init"]
+        assert _rel(dp_got, dp_want) < 2e-2, _rel(dp_got, dp_want)
+        assert np.mean(p != z[f"p{k}_final"]) < 0.05
+
+
+def test_bf16_round_matches_torch():
+    import torch
+    x = np.random.default_rng(0).standard_normal(10000).astype(np.float32) * 7.3
+    x[:4] = [0.0, -0.0, 1e-40, 3.0e38]
+    want = torch.from_numpy(x).bfloat16().float().numpy()
+    np.testing.assert_array_equal(O.bf16_round(x), want)
