@@ -1,0 +1,143 @@
+"""Host-side checks that need no GPU: the C ABI's exports and argument
+validation, the ops-API mirror's error behaviour, and the sharding plan."""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from pytorch_opt_b200 import _lib, native, ops
+from pytorch_opt_b200.dist import ShardLayout, lpt_assign, ns_flops
+from tests.conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "pytorch_opt_b200.h")
+
+
+def _header_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(po_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    names = _header_functions()
+    assert len(names) >= 15
+    for name in names:
+        assert hasattr(lib, name), name
+    # the ctypes binding declares exactly the header's functions
+    assert set(_lib.SIGNATURES) == set(names)
+
+
+def test_load_and_version():
+    lib = _lib.load()
+    assert b"sm_100a" in lib.po_version()
+
+
+def test_abi_rejects_bad_arguments_without_touching_the_device():
+    lib = _lib.load()
+    # bad dtype
+    assert lib.po_newton_schulz(None, 7, 1, 4, 4, 4, 16, None, 4, 16, 5, 3.4, -4.7, 2.0, 1e-7, -1, None, 0,
+                                None) == 1
+    assert "dtype" in _lib.last_error()
+    # negative sizes
+    assert lib.po_newton_schulz(None, 0, 1, -4, 4, 4, 16, None, 4, 16, 5, 3.4, -4.7, 2.0, 1e-7, -1, None, 0,
+                                None) == 1
+    # empty problems are no-ops
+    assert lib.po_newton_schulz(None, 0, 0, 4, 4, 4, 16, None, 4, 16, 5, 3.4, -4.7, 2.0, 1e-7, -1, None, 0,
+                                None) == 0
+    # p must be a positive integer (reference: ValueError / TORCH_CHECK)
+    assert lib.po_inverse_root(None, 0, 1, 4, 4, 16, None, 4, 16, 0, 0.0, 100, 1e-10, None, None, 0, None) == 1
+    assert "positive integer" in _lib.last_error()
+    # workspace too small is reported, not written past
+    assert lib.po_newton_schulz(ctypes.c_void_p(16), 0, 1, 4, 4, 4, 16, ctypes.c_void_p(16), 4, 16, 5, 3.4, -4.7,
+                                2.0, 1e-7, -1, ctypes.c_void_p(256), 8, None) == 3
+    assert "workspace" in _lib.last_error()
+    assert lib.po_matmul(None, 1, 1, 0, None, 1, 1, 0, None, 1, 1, 0, 0, 1, 1, 1, 0, 1.0, 0.0, None, 0, None) == 5
+
+
+def test_workspace_sizes_are_consistent():
+    lib = _lib.load()
+    a = lib.po_ns_workspace_bytes(1, 768, 3072)
+    assert a == lib.po_ns_workspace_bytes(1, 3072, 768)  # transposed problem, same work
+    assert lib.po_ns_workspace_bytes(2, 768, 3072) > a
+    assert lib.po_ns_workspace_bytes(0, 8, 8) == 0
+    r4 = lib.po_root_workspace_bytes(8, 1024, 4)
+    r1 = lib.po_root_workspace_bytes(8, 1024, 1)
+    assert r4 > r1 > 0
+    assert lib.po_syrk_workspace_bytes(8192, 4096, 1) < lib.po_syrk_workspace_bytes(8192, 4096, 0)
+
+
+def test_ops_mirror_argument_errors():
+    A = torch.eye(3)
+    with pytest.raises(ValueError, match="positive integer"):
+        ops.inverse_matrix_root(A, 0)
+    with pytest.raises(ValueError, match="method"):
+        ops.inverse_matrix_root(A, 2, method="qr")
+    with pytest.raises(ValueError, match="ndim"):
+        ops.newton_schulz_orthogonalize(torch.ones(3))
+    with pytest.raises(ValueError, match="2D"):
+        ops.kron_factor_update_(torch.zeros(2, 2), torch.zeros(2, 2), torch.zeros(2, 2, 2))
+
+
+def test_ops_mirror_backend_switch():
+    assert ops.get_backend() == "auto"
+    with pytest.raises(ValueError, match="backend"):
+        ops.set_backend("bogus")
+    with pytest.raises(RuntimeError, match="native backend only"):
+        ops.set_backend("reference")
+    assert ops.load_native() is True and ops.native_available()
+    ops.set_backend("native")
+    assert ops.get_backend() == "native"
+    ops.set_backend("auto")
+
+
+def test_no_cpu_fallback():
+    """CPU tensors are refused loudly: the native path never computes on the host."""
+    ops.load_native()
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        ops.newton_schulz_orthogonalize(torch.randn(8, 5))
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        native.inverse_matrix_root(torch.eye(4), 4, 0.0, "newton", True, 100, 1e-10)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        native.kron_factor_update_(torch.zeros(2, 2), torch.zeros(3, 3), torch.zeros(2, 3), 1.0)
+    with pytest.raises(RuntimeError, match="positive integer"):
+        native.inverse_matrix_root(torch.eye(4), 0, 0.0, "newton", True, 100, 1e-10)
+    with pytest.raises(RuntimeError, match="method"):
+        native.inverse_matrix_root(torch.eye(4), 2, 0.0, "qr", True, 100, 1e-10)
+
+
+LLAMA = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096), (14336, 4096), (4096, 14336)] * 32
+
+
+def test_lpt_assignment_balances_llama_matrices():
+    costs = [ns_flops(r, c) for r, c in LLAMA]
+    for world in (1, 2, 4, 8):
+        plan = lpt_assign(costs, world)
+        assert sorted(i for part in plan for i in part) == list(range(len(LLAMA)))
+        loads = [sum(costs[i] for i in part) for part in plan]
+        assert max(loads) <= sum(costs) / world + max(costs)  # LPT bound
+        assert max(loads) / (sum(costs) / world) < 1.06
+        assert plan == lpt_assign(costs, world)  # deterministic on every rank
+
+
+def test_shard_layout_is_disjoint_and_grouped():
+    shapes = [(64, 96), (96, 64), (64, 96), (32, 32), (64, 96), (16, 48)]
+    for world in (1, 2, 3):
+        lay = ShardLayout(shapes, world)
+        flat = torch.zeros(lay.numel)
+        seen = torch.zeros(lay.numel, dtype=torch.int32)
+        for i, (r, c) in enumerate(shapes):
+            v = lay.matrix(flat, i)
+            assert tuple(v.shape) == (r, c)
+            rank, off = lay.offset_of[i]
+            assert rank * lay.slot <= off and off + r * c <= (rank + 1) * lay.slot
+            seen[off:off + r * c] += 1
+        assert int(seen.max()) == 1
+        for rank in range(world):
+            for g, v in zip(lay.groups[rank], lay.group_views(flat, rank)):
+                assert tuple(v.shape) == (len(g.indices), *g.shape)
+                for k, i in enumerate(g.indices):  # group view k is matrix i
+                    assert v[k].data_ptr() == lay.matrix(flat, i).data_ptr()
