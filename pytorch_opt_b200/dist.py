@@ -27,7 +27,7 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
-from .muon import MuonGroup, muon_group_step, muon_scale
+from .muon import MuonGroup, muon_group_step, muon_scale, ns_workspace_bytes
 
 
 def ns_flops(rows: int, cols: int, steps: int = 5) -> float:
@@ -144,8 +144,12 @@ class ShardedMuon:
         else:
             self.groups = list(zip(pv, gv))
         self._sq = torch.zeros(max(len(self.groups), 1), dtype=torch.float64, device=params_flat.device)
+        self._ws = None
+        if compute is None and self.groups:
+            need = max(ns_workspace_bytes(*g.params.shape) for g in self.groups)
+            self._ws = torch.empty(need, dtype=torch.uint8, device=params_flat.device)
 
-    def local_step(self) -> None:
+    def local_step(self, ns_events: list | None = None) -> None:
         """Update this rank's matrices in place (no communication)."""
         self._sq.zero_()
         if self.compute is not None:
@@ -153,7 +157,7 @@ class ShardedMuon:
                 self.compute(p, g)
             return
         for i, g in enumerate(self.groups):
-            muon_group_step(g, sq_sum=self._sq[i], **self.hp)
+            muon_group_step(g, sq_sum=self._sq[i], workspace=self._ws, ns_events=ns_events, **self.hp)
 
     def exchange(self) -> None:
         """All-gather every rank's updated slot into every rank's parameter buffer."""
@@ -162,9 +166,17 @@ class ShardedMuon:
         local = self.layout.slot_view(self.params_flat, self.rank)
         dist.all_gather_into_tensor(self.params_flat, local, group=self.pg)
 
-    def step(self) -> None:
-        self.local_step()
+    def step(self, ns_events: list | None = None) -> None:
+        self.local_step(ns_events)
         self.exchange()
+
+    def launches_per_step(self) -> int:
+        """Kernels this library launches per local step (the all-gather is NCCL's)."""
+        total = 0
+        for g in self.groups:
+            count = g.params.shape[0] if self.compute is None else g[0].shape[0]
+            total += 2 + (-(-count // 32)) * (2 + 3 * int(self.hp["ns_steps"]))
+        return total
 
     def local_update_sq(self) -> float:
         """Sum over local matrices of eff^2 * sum(O^2) (one host read)."""

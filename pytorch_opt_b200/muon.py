@@ -58,14 +58,24 @@ class MuonGroup:
             self.momentum = torch.zeros_like(self.params)
 
 
+def ns_workspace_bytes(count: int, rows: int, cols: int, max_batch: int = 32) -> int:
+    """Workspace one ``muon_group_step`` call needs (Newton–Schulz on up to ``max_batch`` matrices)."""
+    return int(_lib.load().po_ns_workspace_bytes(min(count, max_batch), rows, cols))
+
+
 def muon_group_step(group: MuonGroup, lr: float = 0.02, momentum: float = 0.95, nesterov: bool = True,
                     ns_steps: int = 5, weight_decay: float = 0.0, lr_adjust: str = "spectral",
-                    sq_sum: torch.Tensor | None = None, coeffs=(3.4445, -4.7750, 2.0315), eps: float = 1e-7) -> None:
+                    sq_sum: torch.Tensor | None = None, coeffs=(3.4445, -4.7750, 2.0315), eps: float = 1e-7,
+                    workspace: torch.Tensor | None = None, max_batch: int = 32, ns_events: list | None = None) -> None:
     """One Muon update of every matrix in ``group`` (in place).
 
     ``sq_sum``: optional fp64 CUDA scalar; receives ``sum(O^2)`` of the
     orthogonalised updates (the reference's ``update_rms`` numerator before
-    the ``eff^2`` factor).
+    the ``eff^2`` factor). ``workspace``: optional uint8 CUDA buffer of at
+    least ``ns_workspace_bytes`` (shared between groups stepped on one
+    stream); Newton–Schulz runs on at most ``max_batch`` matrices per call to
+    bound it. ``ns_events``: optional list; a (start, end) pair of CUDA events
+    recorded around the Newton–Schulz launches is appended (for timing).
     """
     lib = _lib.load()
     p = group.params
@@ -78,19 +88,35 @@ def muon_group_step(group: MuonGroup, lr: float = 0.02, momentum: float = 0.95, 
     stream = _lib.stream_ptr(dev)
     if group._u is None:
         group._u = torch.empty_like(p)
-    nbytes = lib.po_ns_workspace_bytes(count, rows, cols)
-    if group._ws is None or group._ws.numel() < nbytes:
-        group._ws = _lib.workspace(nbytes, dev)
+    nb = min(count, max_batch)
+    nbytes = lib.po_ns_workspace_bytes(nb, rows, cols)
+    if workspace is None:
+        if group._ws is None or group._ws.numel() < nbytes:
+            group._ws = _lib.workspace(nbytes, dev)
+        workspace = group._ws
+    elif workspace.numel() < nbytes:
+        raise ValueError(f"workspace too small: {workspace.numel()} < {nbytes} bytes")
     u = group._u
+    mat = rows * cols
+    es = p.element_size()
     with torch.cuda.device(dev):
         _lib.check(lib.po_muon_momentum(group.grads.data_ptr(), group.momentum.data_ptr(), u.data_ptr(), code, n,
                                         float(momentum), 1 if nesterov else 0, stream), "po_muon_momentum")
         a, b, c = coeffs
         # The orthogonalised update overwrites u in place: Newton–Schulz reads its
         # input only in the packing pass that precedes every product.
-        _lib.check(lib.po_newton_schulz(u.data_ptr(), code, count, rows, cols, cols, rows * cols, u.data_ptr(), cols,
-                                        rows * cols, int(ns_steps), float(a), float(b), float(c), float(eps), -1,
-                                        group._ws.data_ptr(), nbytes, stream), "po_newton_schulz")
+        if ns_events is not None:
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record()
+        for start in range(0, count, max_batch):
+            k = min(max_batch, count - start)
+            ptr = u.data_ptr() + start * mat * es
+            _lib.check(lib.po_newton_schulz(ptr, code, k, rows, cols, cols, mat, ptr, cols, mat, int(ns_steps),
+                                            float(a), float(b), float(c), float(eps), -1, workspace.data_ptr(),
+                                            workspace.numel(), stream), "po_newton_schulz")
+        if ns_events is not None:
+            ev1.record()
+            ns_events.append((ev0, ev1))
         eff = lr * muon_scale(rows, cols, lr_adjust)
         decay = 1.0 - lr * weight_decay if weight_decay else 1.0
         _lib.check(lib.po_muon_apply(p.data_ptr(), u.data_ptr(), code, n, float(eff), float(decay),
@@ -110,11 +136,22 @@ class GroupedMuon:
         dev = groups[0].params.device if groups else torch.device("cuda")
         # One fp64 accumulator of sum(O^2) per group (groups differ in eff).
         self._sq = torch.zeros(max(len(groups), 1), dtype=torch.float64, device=dev)
+        # Groups run one after another on one stream: they share one workspace.
+        need = max((ns_workspace_bytes(*g.params.shape) for g in groups), default=1)
+        self._ws = _lib.workspace(need, dev)
 
     def step(self) -> None:
         self._sq.zero_()
         for i, g in enumerate(self.groups):
-            muon_group_step(g, sq_sum=self._sq[i], **self.hp)
+            muon_group_step(g, sq_sum=self._sq[i], workspace=self._ws, **self.hp)
+
+    def launches_per_step(self) -> int:
+        """Kernels this library launches per ``step()`` (momentum, NS packing + products, update)."""
+        total = 0
+        for g in self.groups:
+            chunks = -(-g.params.shape[0] // 32)
+            total += 2 + chunks * (2 + 3 * int(self.hp["ns_steps"]))
+        return total
 
     def update_rms(self) -> float:
         """``update_rms`` of the last step as ``pytorch_opt/optim/muon.py:92,99`` defines it (one host read)."""
