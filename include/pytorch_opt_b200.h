@@ -71,6 +71,27 @@ int po_newton_schulz(const void* G, int dtype, long long batch, long long rows, 
                      void* stream);
 
 /* ------------------------------------------------------------------------
+ * Newton–Schulz without a caller workspace. No counterpart in the reference:
+ * an addition for callers that cannot allocate device memory — code running
+ * inside a framework that owns all device memory through its own pool (a
+ * cudaMalloc would bypass it and synchronise the device mid-step), or a
+ * plug-in handed device pointers but no allocator. Same arguments and result
+ * as po_newton_schulz, minus the workspace: the library keeps a
+ * PO_NS_STATIC_SCRATCH_BYTES scratch array in device memory on every GPU
+ * that loads it (held until the process exits). Problems whose workspace
+ * (po_ns_workspace_bytes) exceeds it are rejected with PO_ERR_ARG; one
+ * 1024 x 1024 matrix fits. The first call on a device looks up the scratch
+ * address (cudaGetSymbolAddress): make that first call before any stream
+ * capture. Every call on a device uses the same scratch, so calls that
+ * overlap on the GPU (different streams, or different host threads) race;
+ * serialise them. Nothing is allocated or freed.
+ * ---------------------------------------------------------------------- */
+#define PO_NS_STATIC_SCRATCH_BYTES (32u << 20)
+int po_newton_schulz_static(const void* G, int dtype, long long batch, long long rows, long long cols, long long ld,
+                            long long bstride, void* out, long long out_ld, long long out_bstride, int steps,
+                            float a, float b, float c, float eps, int tf32_tail, void* stream);
+
+/* ------------------------------------------------------------------------
  * Inverse p-th root (A_sym + damping I)^(-1/p) by the coupled Newton
  * iteration. Replaces pytorch_opt/ops/csrc/pytorch_opt_ops.cpp:15-39 and
  * :41-63 for method="newton" (bound at :104) and mirrors

@@ -29,6 +29,8 @@ SIGNATURES = {
     "po_ns_workspace_bytes": (_sz, [_ll, _ll, _ll]),
     "po_newton_schulz": (_i, [_vp, _i, _ll, _ll, _ll, _ll, _ll, _vp, _ll, _ll, _i, _f, _f, _f, _f, _i, _vp, _sz,
                               _vp]),
+    "po_newton_schulz_static": (_i, [_vp, _i, _ll, _ll, _ll, _ll, _ll, _vp, _ll, _ll, _i, _f, _f, _f, _f, _i,
+                                     _vp]),
     "po_root_workspace_bytes": (_sz, [_ll, _ll, _i]),
     "po_inverse_root": (_i, [_vp, _i, _ll, _ll, _ll, _ll, _vp, _ll, _ll, _i, _d, _i, _d, _vp, _vp, _sz, _vp]),
     "po_kron_workspace_bytes": (_sz, [_ll, _ll, _i]),
