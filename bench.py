@@ -306,6 +306,196 @@ def run_ours(args, rank, world, local_rank):
     return 0
 
 
+# ------------------------------------------------- secondary workloads (1 GPU)
+def _timed(fn, steps, warmup, dev, flush=None):
+    """Per-call CUDA-event time (ms), L2 flushed between calls (outside the timed intervals)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(dev)
+    clocks.start()
+    pairs = []
+    for _ in range(steps):
+        if flush is not None:
+            flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        pairs.append((a, b))
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    return sum(a.elapsed_time(b) for a, b in pairs) / steps, clk
+
+
+def _line(args, metric, value, unit, hib, workload, tflops, clk, launches, cpu, extra=None):
+    pk = peaks()
+    line = {"metric": metric, "value": round(value, 4), "unit": unit, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": None, "higher_is_better": hib, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": workload, "l2": "flushed between timed calls (256 MiB write)"},
+            "roofline": {"bound": "tensor", "kernel": "tc_gemm_kernel", "achieved": round(tflops, 1),
+                         "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
+                         "frac": round(tflops / pk["bf16_sustained"], 3), "traffic": None,
+                         "peak_source": pk["source"] + " bf16 sustained (MEASURED_PEAKS.json)",
+                         "how": "dense algorithmic FLOPs of the call / its CUDA-event time"},
+            "clocks": clk, "gpu_launches": launches, "e2e": None, "cpu_baseline": cpu}
+    if extra:
+        line.update(extra)
+    print(json.dumps(line), flush=True)
+
+
+def _cpu_time(fn, reps=1):
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
+    fn()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        fn()
+    return (time.perf_counter() - t0) / reps
+
+
+def run_secondary(args, rank):
+    if rank != 0:
+        return 0
+    from pytorch_opt_b200 import native
+    from pytorch_opt_b200.muon import GroupedMuon, MuonGroup
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    try:
+        from oracle import ref_native
+        ref = ref_native.load()
+    except Exception:
+        ref = None
+    threads = len(os.sched_getaffinity(0))
+    w = args.workload
+    if w in ("ns768", "ns4096"):
+        if w == "ns768":   # config 1
+            g = torch.Generator().manual_seed(0)
+            Gc = torch.randn(768, 3072, generator=g)
+            desc, fl = "NS5 of one 768x3072 fp32 matrix, N(0,1), seed 0 (config 1)", ns_flops(768, 3072)
+        else:              # a batch of q/o-shaped matrices: the profiling case of the main workload's products
+            g = torch.Generator().manual_seed(1000)
+            Gc = (torch.randn(4, 4096, 4096, generator=g) * 0.02).bfloat16()
+            desc, fl = "NS5 of 4 x 4096x4096 bf16 matrices (Llama q/o shape), 0.02 N(0,1)", 4 * ns_flops(4096, 4096)
+        G = Gc.to(dev)
+        ms, clk = _timed(lambda: native.newton_schulz_orthogonalize(G, 5, 3.4445, -4.7750, 2.0315, 1e-7),
+                         args.steps, args.warmup, dev, flush)
+        cpu = None
+        if ref is not None and not args.no_cpu_baseline:
+            one = Gc if Gc.dim() == 2 else Gc[0]
+            t = _cpu_time(lambda: ref.newton_schulz_orthogonalize(one, 5, 3.4445, -4.7750, 2.0315, 1e-7))
+            cpu = {"value": round(t * 1e3 * (fl / ns_flops(*one.shape)), 2), "unit": "ms", "cores": threads,
+                   "kind": "reference", "sample": "the reference's ATen NS5 on one matrix of the workload"}
+        m = min(G.shape[-2:])
+        launches = 2 + 3 * 5
+        _line(args, f"{'NS5 768x3072' if w == 'ns768' else 'NS5 4x4096^2'} ms", ms, "ms", False, desc,
+              fl / (ms * 1e-3) / 1e12, clk, launches * args.steps, cpu, {"ms_per_step": round(ms, 4)})
+        return 0
+    if w == "gpt2":        # config 2
+        shapes = [(768, 2304), (768, 768), (768, 3072), (3072, 768)]
+        groups, k = [], 0
+        for shp in shapes:
+            p = torch.empty(12, *shp, dtype=torch.bfloat16, device=dev)
+            gr = torch.empty_like(p)
+            for j in range(12):
+                fill_normal(p[j], 2000 + k, 0.02)
+                fill_normal(gr[j], 1000 + k, 0.02)
+                k += 1
+            groups.append(MuonGroup(p, gr))
+        opt = GroupedMuon(groups, lr=0.02, momentum=0.95, nesterov=True, ns_steps=5)
+        fl = 12 * sum(ns_flops(*s) for s in shapes)
+        ms, clk = _timed(opt.step, args.steps, args.warmup, dev, flush)
+        cpu = None
+        if ref is not None and not args.no_cpu_baseline:
+            gs = (torch.randn(768, 2304) * 0.02).bfloat16()
+            t = _cpu_time(lambda: ref.newton_schulz_orthogonalize(gs, 5, 3.4445, -4.7750, 2.0315, 1e-7))
+            cpu = {"value": round(t * 1e3 * fl / ns_flops(768, 2304), 1), "unit": "ms", "cores": threads,
+                   "kind": "reference", "sample": "the reference's ATen NS5 on one 768x2304 matrix, scaled by FLOPs"}
+        _line(args, "GPT-2-small Muon step ms", ms, "ms", False,
+              "Muon step over 48 GPT-2-small matrices (bf16, 0.02 N(0,1), momentum 0.95 Nesterov, 5 NS steps)",
+              fl / (ms * 1e-3) / 1e12, clk, opt.launches_per_step() * args.steps, cpu,
+              {"ms_per_step": round(ms, 4)})
+        return 0
+    if w == "shampoo":     # config 3
+        res = {}
+        lib_iters = {}
+        for d in (1024, 2048, 4096):
+            g = torch.Generator(device=dev).manual_seed(d * 100)
+            Gs = torch.randn(8, d, 2 * d, generator=g, device=dev)
+            L = Gs @ Gs.mT / (2 * d) + 1e-6 * torch.eye(d, device=dev)
+            del Gs
+            from pytorch_opt_b200 import _lib
+            lib = _lib.load()
+            out = torch.empty_like(L)
+            its = torch.zeros(8, dtype=torch.int32, device=dev)
+            nbytes = lib.po_root_workspace_bytes(8, d, 4)
+            ws = _lib.workspace(nbytes, dev)
+
+            def call():
+                _lib.check(lib.po_inverse_root(L.data_ptr(), 0, 8, d, d, d * d, out.data_ptr(), d, d * d, 4, 1e-8,
+                                               100, 1e-10, its.data_ptr(), ws.data_ptr(), nbytes,
+                                               _lib.stream_ptr(dev)), "root")
+            ms, clk = _timed(call, args.steps, args.warmup, dev, flush)
+            n_it = its.tolist()
+            fl = sum(8.0 * d ** 3 * i for i in n_it)
+            res[d] = {"ms": round(ms, 3), "iters": n_it[0], "tflops": round(fl / (ms * 1e-3) / 1e12, 1)}
+            lib_iters[d] = n_it
+            del L, out, ws
+        cpu = None
+        if ref is not None and not args.no_cpu_baseline:
+            g = torch.Generator().manual_seed(1024 * 100)
+            Gm = torch.randn(1024, 2048, generator=g)
+            Lc = Gm @ Gm.T / 2048 + 1e-6 * torch.eye(1024)
+            t = _cpu_time(lambda: ref.inverse_matrix_root(Lc, 4, 1e-8, "newton", True, 100, 1e-10))
+            cpu = {"value": round(t * 1e3 * 8 * 64, 1), "unit": "ms", "cores": threads, "kind": "reference",
+                   "sample": "the reference's ATen coupled Newton (fp64) on one d=1024 factor, x8 factors x (4096/1024)^3"}
+        _line(args, "Shampoo inverse 4th root TFLOP/s (8 x d=4096)", res[4096]["tflops"], "TFLOP/s", True,
+              "coupled-Newton inverse 4th roots of 8 SPD factors per size, L = G G^T/2d + 1e-6 I, damping 1e-8",
+              res[4096]["tflops"], clk, None, cpu, {"ms_per_step": res[4096]["ms"], "per_size": res})
+        return 0
+    if w == "kfac":        # config 4
+        g1 = torch.Generator(device=dev).manual_seed(1)
+        g2 = torch.Generator(device=dev).manual_seed(2)
+        a = torch.randn(8192, 4096, generator=g1, device=dev).bfloat16()
+        gr = torch.randn(8192, 4096, generator=g2, device=dev).bfloat16()
+        A = torch.empty(4096, 4096, device=dev)
+        Gf = torch.empty(4096, 4096, device=dev)
+        n = 8192
+        native.kron_syrk_ema_(A, a, 1.0 / n, 0.95, True)
+        native.kron_syrk_ema_(Gf, gr, float(n), 0.95, True)
+
+        def update():
+            native.kron_syrk_ema_(A, a, 1.0 / n, 0.95, False)
+            native.kron_syrk_ema_(Gf, gr, float(n), 0.95, False)
+        ms_u, clk = _timed(update, args.steps, args.warmup, dev, flush)
+        tr_a = float(A.diagonal().sum()) / 4096
+        tr_g = float(Gf.diagonal().sum()) / 4096
+        pi = math.sqrt(tr_a / tr_g)
+        ga, gg = pi * math.sqrt(1e-3), math.sqrt(1e-3) / pi
+
+        def inverse():
+            native.damped_inverse(A, ga)
+            native.damped_inverse(Gf, gg)
+        ms_i, _ = _timed(inverse, max(1, args.steps // 2), 1, dev, flush)
+        fl_u = 2 * 2.0 * 8192 * 4096 ** 2
+        cpu = None
+        if not args.no_cpu_baseline:
+            ac = torch.randn(2048, 4096).float()
+            t = _cpu_time(lambda: ac.T @ ac)
+            cpu = {"value": round(t * 1e3 * 4 * 2, 1), "unit": "ms", "cores": threads, "kind": "reference",
+                   "sample": "the reference's factor GEMM (torch fp32 a^T a, kron.py:113) on 2048 of the 8192 rows, "
+                             "x4 rows x2 factors (update only; its fp64 eigh inverse is ~77 s per factor on 8 cores)"}
+        _line(args, "KFAC factor update ms (A and G, 8192x4096 -> 4096^2)", ms_u, "ms", False,
+              "KFAC SYRK+EMA of A = a^T a/n and G = (n g)^T (n g)/n, a, g 8192x4096 bf16, beta 0.95; "
+              "then pi-damped inverses (lambda 1e-3) by coupled Newton p=1",
+              fl_u / (ms_u * 1e-3) / 1e12, clk, None, cpu,
+              {"ms_per_step": round(ms_u, 4), "damped_inverse_ms_both": round(ms_i, 3)})
+        return 0
+    raise SystemExit(f"unknown workload {w}")
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -314,12 +504,17 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="llama8b", choices=("llama8b", "ns768", "ns4096", "gpt2", "shampoo", "kfac"),
+                    help="llama8b (default, config 5); the others are single-GPU measurements of configs 1-4 "
+                         "and the 4x4096^2 profiling case")
     args = ap.parse_args(argv)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference_arm(args, rank, world)
+    if args.workload != "llama8b":
+        return run_secondary(args, rank)
     return run_ours(args, rank, world, local_rank)
 
 
