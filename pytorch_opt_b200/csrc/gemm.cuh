@@ -8,15 +8,16 @@
 // * One elected thread issues tcgen05.mma into a double-buffered TMEM
 //   accumulator (2 x BN fp32 columns), so the epilogue of tile i overlaps the
 //   main loop of tile i+1.
-// * Four epilogue warps drain TMEM with tcgen05.ld and apply a fused
+// * Eight epilogue warps drain TMEM with tcgen05.ld and apply a fused
 //   "alpha*acc + sum(beta_i*C_i) + gamma*I" with up to three typed outputs,
 //   optional mirrored stores (symmetric products computed on the lower
 //   triangle of tiles only) and an optional per-batch max|D - ident*I|.
 // * Split-bf16 ("bf16x3") products: npass = 3 runs the K loop three times,
 //   hi*hi + hi*lo + lo*hi, into the same accumulator.
 //
-// Roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA
-// issuer, warps 2..5 = epilogue (warp w owns TMEM lanes 32*(w%4) .. +31).
+// Roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA
+// issuer, warps 2..9 = epilogue (warp w owns TMEM lanes 32*(w%4) .. +31 and
+// half of the tile's columns: the first half for warps 2..5, the second for 6..9).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -57,6 +58,8 @@ struct EpiOut {
   int zero_diag;  // store 0 on the diagonal (operand copies for the diagonal split)
 };
 
+constexpr int kGemmThreads = 320;                  // 10 warps
+constexpr int kEpilogueThreads = kGemmThreads - 64;  // warps 2..9
 constexpr int kMaxEpiIn = 2;
 constexpr int kMaxEpiOut = 3;
 
@@ -76,6 +79,9 @@ struct Epilogue {
   // the tile reuses the same values.
   int diag_split;
   EpiIn dU, dV;
+  // The addends are exactly symmetric (written by mirrored stores), so the
+  // mirrored half of an off-diagonal tile takes the same values as the tile.
+  int mirror_same;
 };
 
 struct alignas(64) GemmParams {
@@ -323,7 +329,8 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCo
   if (row >= P.M) return;
   const int jd = row - col0;  // diagonal column within this chunk, if any
   float v[EC];
-  if (mirror && !E.diag_split) {
+  const bool same = E.diag_split || E.mirror_same;
+  if (mirror && !same) {
     // Element (row, c) of an off-diagonal tile of a symmetric product is also
     // element (c, row): rebuild it with the addends read at (c, row) and
     // store it there. Off-diagonal tiles hold no diagonal entries.
@@ -374,7 +381,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCo
     for (int j = 0; j < EC; ++j)
       if (col0 + j < N) red_update(red, fabsf(v[j] - (j == jd ? E.red_ident : 0.0f)));
   }
-  if (mirror && E.diag_split) {
+  if (mirror && same) {
     // The full product is symmetric: the mirrored element takes the same value.
 #pragma unroll
     for (int o = 0; o < kMaxEpiOut; ++o)
@@ -391,7 +398,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCo
 constexpr int KCHUNK = 4;
 
 template <int KIND, int BN, bool A_MN, bool B_MN, bool CHUNKED>
-__global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__ GemmParams P) {
+__global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_constant__ GemmParams P) {
   using C = GemmCfg<KIND, BN>;
   constexpr int BM = C::BM;
   static_assert(!CHUNKED || BN == 128, "chunked accumulation keeps a 128-column row in registers");
@@ -417,7 +424,7 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull + a, 1);
-      mbar_init(tempty + a, 128);
+      mbar_init(tempty + a, kEpilogueThreads);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -575,6 +582,8 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
     // -------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    constexpr int HC = BN / EC / 2;        // chunks per column half
+    const int c_lo = ((warp - 2) >> 2) * HC;  // first chunk of this warp's half
     int ucount = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < P.total_tiles && ok; t += gridDim.x) {
@@ -585,9 +594,9 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
       float red = 0.0f;
       if (CHUNKED) {
         const int nv = tile_passes(P, tc.b) * nkb;
-        float racc[BN];
+        float racc[BN / 2];
 #pragma unroll
-        for (int j = 0; j < BN; ++j) racc[j] = 0.0f;
+        for (int j = 0; j < BN / 2; ++j) racc[j] = 0.0f;
         for (int v0 = 0; v0 < nv; v0 += KCHUNK) {
           const int acc = ucount & 1;
           const uint32_t acc_phase = (ucount >> 1) & 1;
@@ -598,9 +607,9 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
           }
           tc_fence_after_sync();
 #pragma unroll
-          for (int c = 0; c < BN / EC; ++c) {
+          for (int c = 0; c < HC; ++c) {
             uint32_t r[EC];
-            tmem_ld_32x16(tmem_base + lane_base + static_cast<uint32_t>(acc * BN + c * EC), r);
+            tmem_ld_32x16(tmem_base + lane_base + static_cast<uint32_t>(acc * BN + (c_lo + c) * EC), r);
             tmem_ld_wait();
 #pragma unroll
             for (int j = 0; j < EC; ++j) racc[c * EC + j] += __uint_as_float(r[j]);
@@ -611,11 +620,11 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
         }
         if (!ok) break;
 #pragma unroll
-        for (int c = 0; c < BN / EC; ++c) {
+        for (int c = 0; c < HC; ++c) {
           float f[EC];
 #pragma unroll
           for (int j = 0; j < EC; ++j) f[j] = racc[c * EC + j];
-          epilogue_chunk(P, tc, row, tc.nt * BN + c * EC, mirror, f, red);
+          epilogue_chunk(P, tc, row, tc.nt * BN + (c_lo + c) * EC, mirror, f, red);
         }
       } else {
         const int acc = ucount & 1;
@@ -625,7 +634,7 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const __grid_constant__
         if (!__all_sync(0xffffffffu, ready)) break;
         tc_fence_after_sync();
 #pragma unroll 1
-        for (int c = 0; c < BN / EC; ++c) {
+        for (int c = c_lo; c < c_lo + HC; ++c) {
           uint32_t r[EC];
           tmem_ld_32x16(tmem_base + lane_base + static_cast<uint32_t>(acc * BN + c * EC), r);
           tmem_ld_wait();

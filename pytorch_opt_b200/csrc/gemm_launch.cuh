@@ -23,7 +23,7 @@ int launch_inst(const GemmParams& P, cudaStream_t stream) {
     configured[dev] = true;
   }
   const int grid = P.total_tiles < sm_count() ? P.total_tiles : sm_count();
-  kern<<<grid, 192, C::SMEM_BYTES, stream>>>(P);
+  kern<<<grid, kGemmThreads, C::SMEM_BYTES, stream>>>(P);
   return check_cuda(cudaGetLastError(), "tc_gemm launch");
 }
 

@@ -192,6 +192,7 @@ extern "C" int po_newton_schulz(const void* G, int dtype, long long batch, long 
     g.b[0] = X.v[0]; g.b[1] = X.v[1];
     g.tri = true;
     g.epi.alpha = 1.0f;
+    g.epi.mirror_same = 1;
     g.epi.out[g.epi.nout++] = epi_out(B.af, OUT_F32, B.ldm, ms);
     add_op_outputs(g.epi, pr, a_hi, a_lo, B.ldm, ms);
     if ((r = launch_gemm(g, s))) return r;
@@ -205,6 +206,7 @@ extern "C" int po_newton_schulz(const void* G, int dtype, long long batch, long 
     q.b[0] = Aop.v[0]; q.b[1] = Aop.v[1];
     q.tri = true;
     q.epi.alpha = c;
+    q.epi.mirror_same = 1;  // A is stored exactly symmetric by the Gram's mirrored stores
     q.epi.nin = 1;
     q.epi.in[0] = epi_in(B.af, IN_F32, B.ldm, ms, b);
     add_op_outputs(q.epi, pr, b_hi, b_lo, B.ldm, ms);
