@@ -3,11 +3,13 @@
 #include <cudaTypedefs.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
 
 #include "gemm_launch.cuh"
+#include "gemm_pair_launch.cuh"
 
 namespace po {
 
@@ -123,6 +125,37 @@ EpiOut epi_out(void* ptr, int out_kind, long long ld, long long bstride, bool tr
   return e;
 }
 
+// Tile shape choice. A one-SM CTA streams 128 x BN operand panels per k-block
+// for its own 128 x BN tile; a pair of SMs computing one 256 x 256 tile
+// streams half as many bytes per SM per MMA, so pair tiles run closer to the
+// tensor-core rate. They are four times larger than 128 x 128 tiles, so on
+// small problems the one-SM kernel can still win by filling more SMs. The
+// estimate: per-SM work of one tile x waves, divided by the measured relative
+// throughput of each tile shape (128x128: 0.55, 128x256: 0.7, pair: 0.85).
+// PO_GEMM_PAIR=0/1 in the environment forces the choice (for measurement).
+static int pair_override() {
+  const char* e = getenv("PO_GEMM_PAIR");
+  if (e == nullptr || *e == 0) return -1;
+  return atoi(e) != 0 ? 1 : 0;
+}
+
+static bool use_pair(const GemmDesc& d, int bn) {
+  int want = d.pair;
+  if (want < 0) want = pair_override();
+  if (want >= 0) return want != 0;
+  const long long sms = sm_count();
+  auto tiles = [&](int tm, int tn) {
+    const long long a = cdiv(d.M, tm), b = cdiv(d.N, tn);
+    return (d.tri ? a * (a + 1) / 2 : a * b) * d.batch;
+  };
+  const long long t1 = tiles(128, bn);
+  const long long t2 = tiles(256, 256);
+  const double eff1 = bn == 256 ? 0.7 : 0.55;
+  const double cost1 = static_cast<double>((t1 + sms - 1) / sms) * 128.0 * bn / eff1;
+  const double cost2 = static_cast<double>((t2 + sms / 2 - 1) / (sms / 2)) * 128.0 * 256.0 / 0.85;
+  return cost2 <= cost1;
+}
+
 int launch_gemm(const GemmDesc& d, cudaStream_t stream) {
   if (d.M <= 0 || d.N <= 0 || d.batch <= 0) return PO_OK;
   if (d.K <= 0) return set_error(PO_ERR_ARG, "launch_gemm: K must be positive");
@@ -136,6 +169,9 @@ int launch_gemm(const GemmDesc& d, cudaStream_t stream) {
   int bn = d.bn;
   if (bn == 0) bn = (d.tri || d.N <= 128) ? 128 : 256;
   if (d.tri || d.chunked) bn = 128;
+  const bool pair = !d.chunked && use_pair(d, bn);
+  const int tm = pair ? 256 : 128;
+  if (pair) bn = 256;
 
   GemmParams P;
   memset(&P, 0, sizeof(P));
@@ -151,7 +187,7 @@ int launch_gemm(const GemmDesc& d, cudaStream_t stream) {
     if (d.a_kmajor) r = encode_map(&P.mapA[i], d.a[src], d.batch, bk, 128);
     else r = encode_map(&P.mapA[i], d.a[src], d.batch, 128 / es, bk, mn_swz);
     if (r) return r;
-    if (d.b_kmajor) r = encode_map(&P.mapB[i], d.b[src], d.batch, bk, bn);
+    if (d.b_kmajor) r = encode_map(&P.mapB[i], d.b[src], d.batch, bk, pair ? bn / 2 : bn);
     else r = encode_map(&P.mapB[i], d.b[src], d.batch, 128 / es, bk, mn_swz);
     if (r) return r;
   }
@@ -159,7 +195,7 @@ int launch_gemm(const GemmDesc& d, cudaStream_t stream) {
   P.N = d.N;
   P.K = d.K;
   P.batch = d.batch;
-  P.tiles_m = cdiv(d.M, 128);
+  P.tiles_m = cdiv(d.M, tm);
   P.tiles_n = cdiv(d.N, bn);
   P.tri = d.tri ? 1 : 0;
   P.tiles_per_batch = d.tri ? P.tiles_m * (P.tiles_m + 1) / 2 : P.tiles_m * P.tiles_n;
@@ -174,6 +210,10 @@ int launch_gemm(const GemmDesc& d, cudaStream_t stream) {
   P.epi = d.epi;
 
   const bool a_mn = !d.a_kmajor, b_mn = !d.b_kmajor;
+  if (pair) {
+    return d.kind == KIND_BF16 ? dispatch_pair<KIND_BF16>(P, a_mn, b_mn, stream)
+                               : dispatch_pair<KIND_TF32>(P, a_mn, b_mn, stream);
+  }
   if (d.chunked) {
     return d.kind == KIND_BF16 ? dispatch_major<KIND_BF16, 128, true>(P, a_mn, b_mn, stream)
                                : dispatch_major<KIND_TF32, 128, true>(P, a_mn, b_mn, stream);

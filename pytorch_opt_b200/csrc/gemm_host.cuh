@@ -30,6 +30,7 @@ struct GemmDesc {
   const int* active = nullptr;
   const int* passes = nullptr;
   int bn = 0;  // 0 = choose
+  int pair = -1;  // two-SM 256 x 256 tiles: 1 = yes, 0 = no, -1 = choose (never with chunked)
   Epilogue epi{};
 };
 
