@@ -77,8 +77,27 @@ def build(force: bool = False, debug: bool = False, verbose: bool = False, jobs:
     srcs = _sources()
     objs = [os.path.join(BUILD_DIR, os.path.basename(s)[:-3] + ".o") for s in srcs]
 
+    hdr_hash = hashlib.sha256()
+    for p in _headers():
+        with open(p, "rb") as f:
+            hdr_hash.update(p.encode())
+            hdr_hash.update(f.read())
+    hdr_hash.update(" ".join(flags).encode())
+
+    def obj_fingerprint(src: str) -> str:
+        h = hdr_hash.copy()
+        with open(src, "rb") as f:
+            h.update(f.read())
+        return h.hexdigest()
+
     def compile_one(pair):
         src, obj = pair
+        ofp = obj_fingerprint(src)
+        ostamp = obj + ".stamp"
+        if not force and os.path.exists(obj) and os.path.exists(ostamp):
+            with open(ostamp) as f:
+                if f.read().strip() == ofp:
+                    return obj  # unchanged since its last compile
         cmd = [nvcc, *flags, "-c", src, "-o", obj]
         if verbose:
             print(" ".join(cmd), flush=True)
@@ -87,11 +106,15 @@ def build(force: bool = False, debug: bool = False, verbose: bool = False, jobs:
             raise RuntimeError(f"nvcc failed on {os.path.basename(src)}:\n{r.stdout}\n{r.stderr}")
         if verbose and (r.stdout or r.stderr):
             print(r.stdout, r.stderr, flush=True)
+        with open(ostamp, "w") as f:
+            f.write(ofp)
         return obj
 
     workers = jobs or min(len(srcs), os.cpu_count() or 4)
+    # The tensor-core GEMM instantiations take longest: start them first.
+    order = sorted(zip(srcs, objs), key=lambda so: (not os.path.basename(so[0]).startswith("gemm_inst"), so[0]))
     with cf.ThreadPoolExecutor(max_workers=workers) as ex:
-        list(ex.map(compile_one, zip(srcs, objs)))
+        list(ex.map(compile_one, order))
     tmp = LIB_PATH + ".tmp"
     cmd = [nvcc, *ARCH_FLAGS, "-shared", "-Xcompiler", "-fPIC", "-o", tmp, *objs]
     r = subprocess.run(cmd, capture_output=True, text=True)

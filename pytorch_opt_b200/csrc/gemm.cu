@@ -101,6 +101,31 @@ static int encode_map(CUtensorMap* map, const MatView& v, int batch, int box_inn
   return PO_OK;
 }
 
+// MN-major operand stored [batch][K][MN] viewed as [batch][MN / w][K][w] with
+// w = 128 B of elements, so that one box {w, box_k, nblk, 1} brings all of a
+// stage's MN blocks in one copy. Only when MN is a multiple of w (the view
+// then covers exactly the stored elements). Returns 1 when not applicable.
+static int encode_map_mn4d(CUtensorMap* map, const MatView& v, int batch, int box_k, int nblk,
+                           CUtensorMapSwizzle swz) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return 1;
+  const int es = dtype_size(v.dtype);
+  const int w = 128 / es;
+  if (v.cols % w != 0 || reinterpret_cast<uintptr_t>(v.ptr) % 16 != 0 || (v.ld * es) % 16 != 0 ||
+      (batch > 1 && (v.bstride * es) % 16 != 0))
+    return 1;
+  const long long bstride_bytes = batch > 1 ? v.bstride * es : v.ld * es * (v.rows > 0 ? v.rows : 1);
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(w), static_cast<cuuint64_t>(v.rows),
+                        static_cast<cuuint64_t>(v.cols / w), static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(v.ld * es), 128, static_cast<cuuint64_t>(bstride_bytes)};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(w), static_cast<cuuint32_t>(box_k), static_cast<cuuint32_t>(nblk), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, v.dtype == PO_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
+                  const_cast<void*>(v.ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : 1;
+}
+
 EpiIn epi_in(const void* ptr, int in_kind, long long ld, long long bstride, float beta) {
   EpiIn e{};
   e.ptr = ptr;
@@ -177,18 +202,31 @@ int launch_gemm(const GemmDesc& d, cudaStream_t stream) {
   memset(&P, 0, sizeof(P));
   const int es = d.kind == KIND_BF16 ? 2 : 4;
   const int bk = 128 / es;
+  // Rows of A and of B one CTA loads per stage.
+  const int a_rows = 128, b_rows = pair ? bn / 2 : bn;
+  // MN-major 32-bit operands: 128 B swizzle with 32 B granules (the only
+  // shared-memory layout the tensor cores accept for MN-major tf32).
+  const CUtensorMapSwizzle mn_swz = es == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+  // PO_GEMM_MN4D=0 in the environment forces the block-by-block loads (for measurement).
+  const char* mn4d_env = getenv("PO_GEMM_MN4D");
+  const bool no_mn4d = d.no_mn4d || (mn4d_env != nullptr && mn4d_env[0] == '0');
+  P.a4d = !d.a_kmajor && !no_mn4d;
+  P.b4d = !d.b_kmajor && !no_mn4d;
+  for (int i = 0; i < nmaps; ++i) {
+    if (P.a4d && encode_map_mn4d(&P.mapA[i], d.a[i], d.batch, bk, a_rows * es / 128, mn_swz)) P.a4d = 0;
+    if (P.b4d && encode_map_mn4d(&P.mapB[i], d.b[i], d.batch, bk, b_rows * es / 128, mn_swz)) P.b4d = 0;
+  }
   for (int i = 0; i < 2; ++i) {
     const int src = i < nmaps ? i : 0;
-    int r;
+    int r = 0;
     // A: logical M x K.
-    // MN-major 32-bit operands: 128 B swizzle with 32 B granules (the only
-    // shared-memory layout the tensor cores accept for MN-major tf32).
-    const CUtensorMapSwizzle mn_swz = es == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
-    if (d.a_kmajor) r = encode_map(&P.mapA[i], d.a[src], d.batch, bk, 128);
-    else r = encode_map(&P.mapA[i], d.a[src], d.batch, 128 / es, bk, mn_swz);
+    if (d.a_kmajor) r = encode_map(&P.mapA[i], d.a[src], d.batch, bk, a_rows);
+    else if (!P.a4d) r = encode_map(&P.mapA[i], d.a[src], d.batch, 128 / es, bk, mn_swz);
+    else if (i >= nmaps) P.mapA[i] = P.mapA[0];
     if (r) return r;
-    if (d.b_kmajor) r = encode_map(&P.mapB[i], d.b[src], d.batch, bk, pair ? bn / 2 : bn);
-    else r = encode_map(&P.mapB[i], d.b[src], d.batch, 128 / es, bk, mn_swz);
+    if (d.b_kmajor) r = encode_map(&P.mapB[i], d.b[src], d.batch, bk, b_rows);
+    else if (!P.b4d) r = encode_map(&P.mapB[i], d.b[src], d.batch, 128 / es, bk, mn_swz);
+    else if (i >= nmaps) P.mapB[i] = P.mapB[0];
     if (r) return r;
   }
   P.M = d.M;

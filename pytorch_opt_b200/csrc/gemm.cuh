@@ -91,6 +91,7 @@ struct alignas(64) GemmParams {
   int tiles_m, tiles_n, tiles_per_batch, total_tiles;
   int tri;    // compute only tiles with nt <= mt (M == N, BN == 128) and mirror-store
   int npass;  // 1 or 3
+  int a4d, b4d;  // MN-major operand mapped as 4-D [batch][MN / (128 B)][K][128 B]: one TMA copy per stage
   const int* active;  // per batch: nonzero = compute (nullable: all)
   const int* passes;  // per batch pass count (nullable: npass)
   int* err;           // device error word
@@ -316,6 +317,35 @@ __device__ __forceinline__ void store_out(const EpiOut& o, int b, int row, int c
   else store_row(o, b, row, col0, ncols, v);
 }
 
+// Ask L2 for the addend bytes of one row segment [col0, col0 + ncols) before
+// the accumulator is ready, so the epilogue's loads hit L2 instead of DRAM.
+__device__ __forceinline__ void prefetch_row_segment(const void* base, int es, long long ld, long long bstride, int b,
+                                                     int row, int col0, int ncols) {
+  if (ncols <= 0) return;
+  const char* p = static_cast<const char*>(base) +
+                  (static_cast<long long>(b) * bstride + static_cast<long long>(row) * ld + col0) * es;
+  const char* end = p + static_cast<long long>(ncols) * es;
+  for (const char* q = reinterpret_cast<const char*>(reinterpret_cast<uintptr_t>(p) & ~uintptr_t(127)); q < end;
+       q += 128)
+    prefetch_l2(q);
+}
+
+// Prefetch every row-oriented addend this thread's epilogue will read for
+// columns [col0, col0 + ncols) of `row`.
+__device__ __forceinline__ void epilogue_prefetch(const GemmParams& P, int b, int row, int col0, int ncols) {
+  const Epilogue& E = P.epi;
+  if (row >= P.M) return;
+  ncols = min(ncols, P.N - col0);
+#pragma unroll
+  for (int i = 0; i < kMaxEpiIn; ++i)
+    if (i < E.nin) prefetch_row_segment(E.in[i].ptr, E.in[i].kind == IN_F32 ? 4 : 2, E.in[i].ld, E.in[i].bstride, b, row,
+                                        col0, ncols);
+  if (E.diag_split) {
+    prefetch_row_segment(E.dU.ptr, 4, E.dU.ld, E.dU.bstride, b, row, col0, ncols);
+    prefetch_row_segment(E.dV.ptr, 4, E.dV.ld, E.dV.bstride, b, row, col0, ncols);
+  }
+}
+
 // Running max of |values| for the convergence test; NaN counts as +inf.
 __device__ __forceinline__ void red_update(float& red, float d) {
   red = (d != d) ? __int_as_float(0x7f800000) : fmaxf(red, d);
@@ -470,6 +500,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
           uint8_t* sb = sa + C::A_BYTES;
           if (!A_MN) {
             tma_load_3d(sa, ma, full + stage, k0, tc.mt * BM, tc.b);
+          } else if (P.a4d) {
+            tma_load_4d(sa, ma, full + stage, 0, k0, tc.mt * BM / (128 / C::ES), tc.b);
           } else {
 #pragma unroll
             for (int i = 0; i < BM * C::ES / 128; ++i)
@@ -477,6 +509,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
           }
           if (!B_MN) {
             tma_load_3d(sb, mb, full + stage, k0, tc.nt * BN, tc.b);
+          } else if (P.b4d) {
+            tma_load_4d(sb, mb, full + stage, 0, k0, tc.nt * BN / (128 / C::ES), tc.b);
           } else {
 #pragma unroll
             for (int i = 0; i < BN * C::ES / 128; ++i)
@@ -544,7 +578,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
               ok = false;
               break;
             }
-            tc_fence_after_sync();
+            // TMA writes and tensor-core reads are both async-proxy operations ordered
+            // by the mbarrier: no tcgen05 fence is needed between them.
             const uint32_t sa = smem_u32(tiles + stage * C::STAGE_BYTES);
             const uint32_t sb = sa + C::A_BYTES;
 #pragma unroll
@@ -592,6 +627,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
       const int row = tc.mt * BM + q * 32 + lane;
       const bool mirror = P.tri && tc.mt != tc.nt;
       float red = 0.0f;
+      epilogue_prefetch(P, tc.b, row, tc.nt * BN + c_lo * EC, HC * EC);
       if (CHUNKED) {
         const int nv = tile_passes(P, tc.b) * nkb;
         float racc[BN / 2];

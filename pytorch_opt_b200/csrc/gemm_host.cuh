@@ -31,6 +31,7 @@ struct GemmDesc {
   const int* passes = nullptr;
   int bn = 0;  // 0 = choose
   int pair = -1;  // two-SM 256 x 256 tiles: 1 = yes, 0 = no, -1 = choose (never with chunked)
+  bool no_mn4d = false;  // load MN-major operands block by block (3-D maps) instead of one 4-D copy
   Epilogue epi{};
 };
 

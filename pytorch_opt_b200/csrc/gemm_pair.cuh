@@ -27,7 +27,7 @@ struct PairCfg {
   static constexpr int A_BYTES = 128 * 128;               // this CTA's 128 rows of A
   static constexpr int B_BYTES = (BN / 2) * 128;          // this CTA's half of B
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // per CTA
-  static constexpr int STAGES = 6;
+  static constexpr int STAGES = 7;
   static constexpr int MMA_K = (KIND == KIND_BF16) ? 16 : 8;
   static constexpr int KSTEPS = BK / MMA_K;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
@@ -118,6 +118,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
           uint8_t* sb = sa + C::A_BYTES;
           if (!A_MN) {
             tma_load_3d_pair(sa, ma, bar, k0, arow, tc.b);
+          } else if (P.a4d) {
+            tma_load_4d_pair(sa, ma, bar, 0, k0, arow / (128 / C::ES), tc.b);
           } else {
 #pragma unroll
             for (int i = 0; i < 128 * C::ES / 128; ++i)
@@ -125,6 +127,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
           }
           if (!B_MN) {
             tma_load_3d_pair(sb, mb, bar, k0, brow, tc.b);
+          } else if (P.b4d) {
+            tma_load_4d_pair(sb, mb, bar, 0, k0, brow / (128 / C::ES), tc.b);
           } else {
 #pragma unroll
             for (int i = 0; i < (BN / 2) * C::ES / 128; ++i)
@@ -184,7 +188,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
             ok = false;
             break;
           }
-          tc_fence_after_sync();
+          // TMA writes and tensor-core reads are both async-proxy operations ordered
+          // by the mbarrier: no tcgen05 fence is needed between them.
           const uint32_t sa = smem_u32(tiles + stage * C::STAGE_BYTES);
           const uint32_t sb = sa + C::A_BYTES;
 #pragma unroll
@@ -229,6 +234,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
       const int row = tc.mt * C::TM + static_cast<int>(rank) * 128 + q * 32 + lane;
       const bool mirror = P.tri && tc.mt != tc.nt;
       float red = 0.0f;
+      epilogue_prefetch(P, tc.b, row, tc.nt * BN + c_lo * EC, HC * EC);
       const int acc = ucount & 1;
       const uint32_t acc_phase = (ucount >> 1) & 1;
       const bool ready = mbar_wait_bounded(tfull + acc, acc_phase, abort_flag, P.err, kErrTimeoutEpilogue);
