@@ -210,24 +210,23 @@ __device__ __forceinline__ void add_row(const EpiIn& in, int b, int row, int col
 
 // x[j] += beta * in(col0 + j, row): the transposed position (coalesced
 // across the warp, whose lanes hold consecutive rows).
-__device__ __forceinline__ void add_col(const EpiIn& in, int b, int row, int col0, int ncols, float (&x)[EC]) {
-  const long long base = static_cast<long long>(b) * in.bstride + row;
-  const float beta = in.beta;
+template <typename T>
+__device__ __forceinline__ void add_col_typed(const T* p, long long ld, int nv, float beta, float (&x)[EC]) {
+  if (nv >= EC) {
 #pragma unroll
-  for (int j = 0; j < EC; ++j) {
-    if (col0 + j < ncols) {
-      const long long off = base + static_cast<long long>(col0 + j) * in.ld;
-      const float v = (in.kind == IN_F32) ? static_cast<const float*>(in.ptr)[off]
-                                          : __bfloat162float(static_cast<const __nv_bfloat16*>(in.ptr)[off]);
-      x[j] += beta * v;
-    }
+    for (int j = 0; j < EC; ++j) x[j] += beta * static_cast<float>(p[j * ld]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < EC; ++j)
+      if (j < nv) x[j] += beta * static_cast<float>(p[j * ld]);
   }
 }
 
-__device__ __forceinline__ float convert_out(int kind, float v) {
-  if (kind == OUT_TF32) return round_tf32(v);
-  if (kind == OUT_BF16_LO) return bf16_lo(v);
-  return v;
+__device__ __forceinline__ void add_col(const EpiIn& in, int b, int row, int col0, int ncols, float (&x)[EC]) {
+  const long long off = static_cast<long long>(b) * in.bstride + row + static_cast<long long>(col0) * in.ld;
+  const int nv = ncols - col0;
+  if (in.kind == IN_F32) add_col_typed(static_cast<const float*>(in.ptr) + off, in.ld, nv, in.beta, x);
+  else add_col_typed(static_cast<const __nv_bfloat16*>(in.ptr) + off, in.ld, nv, in.beta, x);
 }
 
 __device__ __forceinline__ void store_elem(const EpiOut& o, long long off, float v) {
@@ -242,34 +241,42 @@ __device__ __forceinline__ void store_elem(const EpiOut& o, long long off, float
 }
 
 // Store EC values of row `row` at columns col0.. (row-major orientation).
+template <typename Cvt>
+__device__ __forceinline__ void store_row_f32x4(float* p, const float (&v)[EC], Cvt cvt) {
+#pragma unroll
+  for (int q = 0; q < EC / 4; ++q)
+    reinterpret_cast<float4*>(p)[q] = make_float4(cvt(v[4 * q]), cvt(v[4 * q + 1]), cvt(v[4 * q + 2]), cvt(v[4 * q + 3]));
+}
+template <typename Cvt>
+__device__ __forceinline__ void store_row_bf16x8(__nv_bfloat16* p, const float (&v)[EC], Cvt cvt) {
+#pragma unroll
+  for (int q = 0; q < EC / 8; ++q) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(cvt(v[8 * q + 2 * e]), cvt(v[8 * q + 2 * e + 1]));
+    reinterpret_cast<uint4*>(p)[q] = u;
+  }
+}
+
 __device__ __forceinline__ void store_row(const EpiOut& o, int b, int row, int col0, int ncols, const float (&v)[EC]) {
   const long long base = static_cast<long long>(b) * o.bstride + static_cast<long long>(row) * o.ld + col0;
   if (o.vec && col0 + EC <= ncols) {
-    if (o.kind == OUT_F32 || o.kind == OUT_TF32) {
-      float4* p = reinterpret_cast<float4*>(static_cast<float*>(o.ptr) + base);
-#pragma unroll
-      for (int q = 0; q < EC / 4; ++q) {
-        float4 f;
-        f.x = convert_out(o.kind, v[4 * q]);
-        f.y = convert_out(o.kind, v[4 * q + 1]);
-        f.z = convert_out(o.kind, v[4 * q + 2]);
-        f.w = convert_out(o.kind, v[4 * q + 3]);
-        p[q] = f;
-      }
-      return;
-    }
-    if (o.kind == OUT_BF16 || o.kind == OUT_BF16_LO) {
-      uint4* p = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(o.ptr) + base);
-#pragma unroll
-      for (int q = 0; q < EC / 8; ++q) {
-        uint4 u;
-        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          h[e] = __floats2bfloat162_rn(convert_out(o.kind, v[8 * q + 2 * e]), convert_out(o.kind, v[8 * q + 2 * e + 1]));
-        p[q] = u;
-      }
-      return;
+    switch (o.kind) {
+      case OUT_F32:
+        store_row_f32x4(static_cast<float*>(o.ptr) + base, v, [](float x) { return x; });
+        return;
+      case OUT_TF32:
+        store_row_f32x4(static_cast<float*>(o.ptr) + base, v, [](float x) { return round_tf32(x); });
+        return;
+      case OUT_BF16:
+        store_row_bf16x8(static_cast<__nv_bfloat16*>(o.ptr) + base, v, [](float x) { return x; });
+        return;
+      case OUT_BF16_LO:
+        store_row_bf16x8(static_cast<__nv_bfloat16*>(o.ptr) + base, v, [](float x) { return bf16_lo(x); });
+        return;
+      default:
+        break;
     }
   }
 #pragma unroll
@@ -277,12 +284,46 @@ __device__ __forceinline__ void store_row(const EpiOut& o, int b, int row, int c
     if (col0 + j < ncols) store_elem(o, base + j, v[j]);
 }
 
-// Store element (row, col0+j) at the transposed position [col0+j][row].
-__device__ __forceinline__ void store_col(const EpiOut& o, int b, int row, int col0, int ncols, const float (&v)[EC]) {
-  const long long base = static_cast<long long>(b) * o.bstride + row;
+// Store element (row, col0+j) at the transposed position [col0+j][row]: one
+// store per column, coalesced across the warp. The output kind is resolved
+// once per chunk, not per element.
+template <typename T, typename Cvt>
+__device__ __forceinline__ void store_col_typed(T* p, long long ld, int nv, const float (&v)[EC], Cvt cvt) {
+  if (nv >= EC) {
 #pragma unroll
-  for (int j = 0; j < EC; ++j)
-    if (col0 + j < ncols) store_elem(o, base + static_cast<long long>(col0 + j) * o.ld, v[j]);
+    for (int j = 0; j < EC; ++j) p[j * ld] = cvt(v[j]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < EC; ++j)
+      if (j < nv) p[j * ld] = cvt(v[j]);
+  }
+}
+
+__device__ __forceinline__ void store_col(const EpiOut& o, int b, int row, int col0, int ncols, const float (&v)[EC]) {
+  const long long off = static_cast<long long>(b) * o.bstride + row + static_cast<long long>(col0) * o.ld;
+  const int nv = ncols - col0;
+  switch (o.kind) {
+    case OUT_F32:
+      store_col_typed(static_cast<float*>(o.ptr) + off, o.ld, nv, v, [](float x) { return x; });
+      break;
+    case OUT_TF32:
+      store_col_typed(static_cast<float*>(o.ptr) + off, o.ld, nv, v, [](float x) { return round_tf32(x); });
+      break;
+    case OUT_BF16:
+      store_col_typed(static_cast<__nv_bfloat16*>(o.ptr) + off, o.ld, nv, v,
+                      [](float x) { return __float2bfloat16_rn(x); });
+      break;
+    case OUT_BF16_LO:
+      store_col_typed(static_cast<__nv_bfloat16*>(o.ptr) + off, o.ld, nv, v,
+                      [](float x) { return __float2bfloat16_rn(bf16_lo(x)); });
+      break;
+    case OUT_F64:
+      store_col_typed(static_cast<double*>(o.ptr) + off, o.ld, nv, v, [](float x) { return static_cast<double>(x); });
+      break;
+    default:
+      store_col_typed(static_cast<__half*>(o.ptr) + off, o.ld, nv, v, [](float x) { return __float2half_rn(x); });
+      break;
+  }
 }
 
 // Load EC consecutive fp32 elements of row `row` (zeros past ncols).
@@ -636,7 +677,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
         for (int v0 = 0; v0 < nv; v0 += KCHUNK) {
           const int acc = ucount & 1;
           const uint32_t acc_phase = (ucount >> 1) & 1;
-          const bool ready = mbar_wait_bounded(tfull + acc, acc_phase, abort_flag, P.err, kErrTimeoutEpilogue);
+          const bool ready = mbar_wait_bounded_sleep(tfull + acc, acc_phase, abort_flag, P.err, kErrTimeoutEpilogue);
           if (!__all_sync(0xffffffffu, ready)) {
             ok = false;
             break;
@@ -666,7 +707,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
         const int acc = ucount & 1;
         const uint32_t acc_phase = (ucount >> 1) & 1;
         // Keep the warp converged for tcgen05.ld: leave together if any lane gave up.
-        const bool ready = mbar_wait_bounded(tfull + acc, acc_phase, abort_flag, P.err, kErrTimeoutEpilogue);
+        const bool ready = mbar_wait_bounded_sleep(tfull + acc, acc_phase, abort_flag, P.err, kErrTimeoutEpilogue);
         if (!__all_sync(0xffffffffu, ready)) break;
         tc_fence_after_sync();
 #pragma unroll 1

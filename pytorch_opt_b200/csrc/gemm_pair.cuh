@@ -237,7 +237,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
       epilogue_prefetch(P, tc.b, row, tc.nt * BN + c_lo * EC, HC * EC);
       const int acc = ucount & 1;
       const uint32_t acc_phase = (ucount >> 1) & 1;
-      const bool ready = mbar_wait_bounded(tfull + acc, acc_phase, abort_flag, P.err, kErrTimeoutEpilogue);
+      const bool ready = mbar_wait_bounded_sleep(tfull + acc, acc_phase, abort_flag, P.err, kErrTimeoutEpilogue);
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after_sync();
 #pragma unroll 1

@@ -84,6 +84,38 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// try_wait with a suspend-time hint: the thread may sleep up to `hint_ns`
+// (it resumes when the phase completes) instead of spinning.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for roles that wait for long stretches (the epilogue waits a
+// whole main loop for its accumulator): sleeps in the barrier, with the same
+// timeout and abort semantics as mbar_wait_bounded.
+__device__ __forceinline__ bool mbar_wait_bounded_sleep(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                        int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+      *abort_flag = 1;
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
 // --------------------------------------------------------------------- TMA
 // 3-D tiled bulk tensor load global -> shared, completing on an mbarrier.
 // No multicast: each CTA fetches its own tiles.
