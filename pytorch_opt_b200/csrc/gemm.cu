@@ -236,6 +236,12 @@ int launch_gemm(const GemmDesc& d, cudaStream_t stream) {
   P.tiles_m = cdiv(d.M, tm);
   P.tiles_n = cdiv(d.N, bn);
   P.tri = d.tri ? 1 : 0;
+  // Raster band height and A residency hint; PO_GEMM_GROUP / PO_GEMM_AKEEP in
+  // the environment override them (for measurement).
+  P.group = 8;
+  P.a_keep = 0;
+  if (const char* e = getenv("PO_GEMM_GROUP")) P.group = atoi(e) > 0 ? atoi(e) : 8;
+  if (const char* e = getenv("PO_GEMM_AKEEP")) P.a_keep = atoi(e) != 0;
   P.tiles_per_batch = d.tri ? P.tiles_m * (P.tiles_m + 1) / 2 : P.tiles_m * P.tiles_n;
   const long long total = static_cast<long long>(P.tiles_per_batch) * d.batch;
   if (total > 0x7fffffffLL) return set_error(PO_ERR_ARG, "launch_gemm: too many tiles");
@@ -243,6 +249,9 @@ int launch_gemm(const GemmDesc& d, cudaStream_t stream) {
   P.npass = d.npass;
   P.active = d.active;
   P.passes = d.passes;
+  // PO_GEMM_DYN=0 in the environment forces the static schedule (for measurement).
+  const char* dyn_env = getenv("PO_GEMM_DYN");
+  P.sched = (pair && !(dyn_env != nullptr && dyn_env[0] == '0')) ? d.sched : nullptr;
   P.err = device_error_word();
   if (P.err == nullptr) return set_error(PO_ERR_CUDA, "device error word unavailable");
   P.epi = d.epi;

@@ -92,6 +92,9 @@ struct alignas(64) GemmParams {
   int tri;    // compute only tiles with nt <= mt (M == N, BN == 128) and mirror-store
   int npass;  // 1 or 3
   int a4d, b4d;  // MN-major operand mapped as 4-D [batch][MN / (128 B)][K][128 B]: one TMA copy per stage
+  int group;     // row tiles per raster band (tiles of a band share A panels through L2)
+  unsigned int* sched;  // {next tile, CTAs finished}: dynamic tile queue (two-SM kernel), null = static
+  int a_keep;    // load A with the L2 evict-last policy (its panels are re-read across the band)
   const int* active;  // per batch: nonzero = compute (nullable: all)
   const int* passes;  // per batch pass count (nullable: npass)
   int* err;           // device error word
@@ -132,7 +135,7 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmParams& P, int t) {
   } else {
     // Rasterise in bands of 8 row-tiles so concurrently running CTAs share
     // operand panels in L2.
-    const int GROUP = 8;
+    const int GROUP = P.group;
     const int band = r / (GROUP * P.tiles_n);
     const int first = band * GROUP;
     const int rows = min(P.tiles_m - first, GROUP);
@@ -518,6 +521,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------ TMA producer
+      const uint64_t keep = policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -540,9 +544,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
           uint8_t* sa = tiles + stage * C::STAGE_BYTES;
           uint8_t* sb = sa + C::A_BYTES;
           if (!A_MN) {
-            tma_load_3d(sa, ma, full + stage, k0, tc.mt * BM, tc.b);
+            if (P.a_keep) tma_load_3d_hint(sa, ma, full + stage, k0, tc.mt * BM, tc.b, keep);
+            else tma_load_3d(sa, ma, full + stage, k0, tc.mt * BM, tc.b);
           } else if (P.a4d) {
-            tma_load_4d(sa, ma, full + stage, 0, k0, tc.mt * BM / (128 / C::ES), tc.b);
+            if (P.a_keep) tma_load_4d_hint(sa, ma, full + stage, 0, k0, tc.mt * BM / (128 / C::ES), tc.b, keep);
+            else tma_load_4d(sa, ma, full + stage, 0, k0, tc.mt * BM / (128 / C::ES), tc.b);
           } else {
 #pragma unroll
             for (int i = 0; i < BM * C::ES / 128; ++i)

@@ -31,7 +31,11 @@ struct GemmDesc {
   const int* passes = nullptr;
   int bn = 0;  // 0 = choose
   int pair = -1;  // two-SM 256 x 256 tiles: 1 = yes, 0 = no, -1 = choose (never with chunked)
-  bool no_mn4d = false;  // load MN-major operands block by block (3-D maps) instead of one 4-D copy
+  bool no_mn4d = false;
+  // Tile queue of the two-SM kernel: 8 bytes of the caller's workspace, zero
+  // before the first launch that uses them (each launch leaves them zero for
+  // the next one on the same stream). Null: static round-robin schedule.
+  unsigned int* sched = nullptr;  // load MN-major operands block by block (3-D maps) instead of one 4-D copy
   Epilogue epi{};
 };
 
@@ -40,5 +44,11 @@ EpiIn epi_in(const void* ptr, int in_kind, long long ld, long long bstride, floa
 EpiOut epi_out(void* ptr, int out_kind, long long ld, long long bstride, bool trans = false);
 
 int launch_gemm(const GemmDesc& d, cudaStream_t stream);
+
+// Tile-queue words for GemmDesc::sched, carved from an op's workspace.
+inline unsigned int* take_sched(Arena& ar) { return static_cast<unsigned int*>(ar.take(8)); }
+inline int zero_sched(unsigned int* q, cudaStream_t s) {
+  return q == nullptr ? PO_OK : check_cuda(cudaMemsetAsync(q, 0, 8, s), "memset");
+}
 
 }  // namespace po

@@ -31,11 +31,34 @@ struct PairCfg {
   static constexpr int MMA_K = (KIND == KIND_BF16) ? 16 : 8;
   static constexpr int KSTEPS = BK / MMA_K;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 512;
   static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
 constexpr int kPairEpilogueWarps = 16;  // eight per CTA, each releases once per tile
+
+// Tile queue. The leader's producer thread takes tile indices from a global
+// counter (P.sched) in the order the pairs become free, so the tiles in flight
+// always form one contiguous window of the raster and share their operand
+// panels through L2 (a fixed round-robin lets pairs drift apart). Each index
+// is published through a ring of kSchedSlots entries in both CTAs' shared
+// memory; a slot is reused once all its readers have released it.
+constexpr int kSchedSlots = 4;
+// Readers of each slot: leader MMA issuer + 8 leader epilogue warps, peer
+// producer + 8 peer epilogue warps.
+constexpr int kSchedReaders = 2 + kPairEpilogueWarps;
+
+// Reader side of the tile queue: index of the j-th tile this pair works on.
+__device__ __forceinline__ bool sched_read(uint64_t* sfull, const int* stile, int j, volatile int* abort_flag,
+                                           int* err, int code, int& t) {
+  const int slot = j % kSchedSlots;
+  if (!mbar_wait_bounded_cluster(sfull + slot, (j / kSchedSlots) & 1u, abort_flag, err, code)) return false;
+  t = *reinterpret_cast<const volatile int*>(stile + slot);
+  return true;
+}
+__device__ __forceinline__ void sched_release(uint64_t* sempty, int j) {
+  mbar_arrive_cluster(mapa_shared(smem_u32(sempty + j % kSchedSlots), 0));
+}
 
 template <int KIND, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __grid_constant__ GemmParams P) {
@@ -50,7 +73,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* sfull = drain + 1;               // [kSchedSlots] tile index published
+  uint64_t* sempty = sfull + kSchedSlots;    // [kSchedSlots] all readers done (leader's copy is used)
+  int* stile = reinterpret_cast<int*>(sempty + kSchedSlots);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(stile + kSchedSlots);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -70,6 +96,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
       mbar_init(tempty + a, kPairEpilogueWarps);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < kSchedSlots; ++i) {
+      mbar_init(sfull + i, 1);
+      mbar_init(sempty + i, kSchedReaders);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -90,11 +120,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------ TMA producer (both CTAs)
+      const uint64_t keep = policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       uint32_t armed = 0;
-      for (int t = pair; t < P.total_tiles && ok; t += npairs) {
+      for (int j = 0; ok; ++j) {
+        int t;
+        if (leader) {
+          // Take the next tile and publish it to both CTAs.
+          const int slot = j % kSchedSlots;
+          if (!mbar_wait_bounded_cluster(sempty + slot, ((j / kSchedSlots) & 1u) ^ 1u, abort_flag, P.err,
+                                         kErrTimeoutProducer))
+            break;
+          t = P.sched != nullptr ? static_cast<int>(atomicAdd(P.sched, 1u)) : pair + j * npairs;
+          stile[slot] = t;
+          st_shared_cluster_u32(mapa_shared(smem_u32(stile + slot), 1), static_cast<uint32_t>(t));
+          mbar_arrive(sfull + slot);
+          mbar_arrive_cluster(mapa_shared(smem_u32(sfull + slot), 1));
+        } else {
+          if (!sched_read(sfull, stile, j, abort_flag, P.err, kErrTimeoutProducer, t)) break;
+          sched_release(sempty, j);
+        }
+        if (t >= P.total_tiles) break;
         const TileCoord tc = decode_tile(P, t);
         if (!tile_active(P, tc.b)) continue;
         const int nv = tile_passes(P, tc.b) * nkb;
@@ -117,9 +165,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
           uint8_t* sa = tiles + stage * C::STAGE_BYTES;
           uint8_t* sb = sa + C::A_BYTES;
           if (!A_MN) {
-            tma_load_3d_pair(sa, ma, bar, k0, arow, tc.b);
+            if (P.a_keep) tma_load_3d_pair_hint(sa, ma, bar, k0, arow, tc.b, keep);
+            else tma_load_3d_pair(sa, ma, bar, k0, arow, tc.b);
           } else if (P.a4d) {
-            tma_load_4d_pair(sa, ma, bar, 0, k0, arow / (128 / C::ES), tc.b);
+            if (P.a_keep) tma_load_4d_pair_hint(sa, ma, bar, 0, k0, arow / (128 / C::ES), tc.b, keep);
+            else tma_load_4d_pair(sa, ma, bar, 0, k0, arow / (128 / C::ES), tc.b);
           } else {
 #pragma unroll
             for (int i = 0; i < 128 * C::ES / 128; ++i)
@@ -174,7 +224,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
       uint32_t phase = 0;
       int ucount = 0;
       bool ok = true;
-      for (int t = pair; t < P.total_tiles && ok; t += npairs) {
+      for (int j = 0; ok; ++j) {
+        int t;
+        if (!sched_read(sfull, stile, j, abort_flag, P.err, kErrTimeoutMma, t)) break;
+        sched_release(sempty, j);
+        if (t >= P.total_tiles) break;
         const TileCoord tc = decode_tile(P, t);
         if (!tile_active(P, tc.b)) continue;
         const int nv = tile_passes(P, tc.b) * nkb;
@@ -228,7 +282,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
     constexpr int HC = BN / EC / 2;
     const int c_lo = ((warp - 2) >> 2) * HC;
     int ucount = 0;
-    for (int t = pair; t < P.total_tiles; t += npairs) {
+    for (int j = 0;; ++j) {
+      int t;
+      const bool got = sched_read(sfull, stile, j, abort_flag, P.err, kErrTimeoutEpilogue, t);
+      if (!__all_sync(0xffffffffu, got)) break;
+      __syncwarp();
+      if (lane == 0) sched_release(sempty, j);
+      if (t >= P.total_tiles) break;
       const TileCoord tc = decode_tile(P, t);
       if (!tile_active(P, tc.b)) continue;
       const int row = tc.mt * C::TM + static_cast<int>(rank) * 128 + q * 32 + lane;
@@ -269,6 +329,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
   if (warp == 1) {
     tc_fence_after_sync();
     tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && P.sched != nullptr) {
+    // The last CTA to finish re-arms the queue for the next launch that uses it.
+    __threadfence();
+    if (atomicAdd(P.sched + 1, 1u) == gridDim.x - 1) {
+      atomicExch(P.sched, 0u);
+      atomicExch(P.sched + 1, 0u);
+    }
   }
 }
 

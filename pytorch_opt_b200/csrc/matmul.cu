@@ -95,6 +95,7 @@ extern "C" int po_matmul(const void* A, long long lda, long long sa, int trans_a
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const Stored sta = stored(M, K, trans_a), stb = stored(K, N, trans_b);
   Arena ar(workspace, workspace_bytes);
+  unsigned int* sched = take_sched(ar);
   const Staged ga = stage_layout(ar, batch, sta);
   const Staged gb = stage_layout(ar, batch, stb);
   if (workspace == nullptr || ar.overflow()) return set_error(PO_ERR_WORKSPACE, "matmul: workspace too small");
@@ -110,7 +111,9 @@ extern "C" int po_matmul(const void* A, long long lda, long long sa, int trans_a
   g.kind = (dtype == PO_BF16 || split) ? KIND_BF16 : KIND_TF32;
   g.npass = split ? 3 : 1;
   g.chunked = split;  // the precise mode also sums K chunks outside the truncating accumulator
+  g.sched = sched;
   int r;
+  if ((r = zero_sched(sched, s))) return r;
   if ((r = prepare_operand(A, dtype, lda, sa, sta, batch, split, ga, g.a, s))) return r;
   if ((r = prepare_operand(B, dtype, ldb, sb, stb, batch, split, gb, g.b, s))) return r;
   g.epi.alpha = alpha;

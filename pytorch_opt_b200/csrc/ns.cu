@@ -36,6 +36,7 @@ struct NsBuffers {
   char* aop;                // A as product operand: fp32 (tf32) or bf16 hi | bf16 lo
   char* bop;                // B as product operand, same layout
   double* sums;             // per-matrix sum of squares
+  unsigned int* sched;      // tile queue of the products
   long long ldx, ldm, msz;  // msz: elements of one [batch][m][ldm] array
 };
 
@@ -53,6 +54,7 @@ void ns_layout(Arena& ar, long long batch, long long m, long long n, bool split,
   B.aop = static_cast<char*>(ar.take(ms * 4));
   B.bop = static_cast<char*>(ar.take(ms * 4));
   B.sums = static_cast<double*>(ar.take(static_cast<size_t>(batch) * 8));
+  B.sched = take_sched(ar);
 }
 
 int out_kind_of(int dtype) {
@@ -156,6 +158,7 @@ extern "C" int po_newton_schulz(const void* G, int dtype, long long batch, long 
 
   int r = check_cuda(cudaMemsetAsync(B.sums, 0, static_cast<size_t>(batch) * 8, s), "memset");
   if (r) return r;
+  if ((r = zero_sched(B.sched, s))) return r;
   AnyMat src{G, dtype, rows, cols, ld, bstride};
   if ((r = launch_sumsq(src, static_cast<int>(batch), B.sums, s))) return r;
   const Prec p0 = prec_of(0);
@@ -191,6 +194,7 @@ extern "C" int po_newton_schulz(const void* G, int dtype, long long batch, long 
     g.a[0] = X.v[0]; g.a[1] = X.v[1];
     g.b[0] = X.v[0]; g.b[1] = X.v[1];
     g.tri = true;
+    g.sched = B.sched;
     g.epi.alpha = 1.0f;
     g.epi.mirror_same = 1;
     g.epi.out[g.epi.nout++] = epi_out(B.af, OUT_F32, B.ldm, ms);
@@ -205,6 +209,7 @@ extern "C" int po_newton_schulz(const void* G, int dtype, long long batch, long 
     q.a[0] = Aop.v[0]; q.a[1] = Aop.v[1];
     q.b[0] = Aop.v[0]; q.b[1] = Aop.v[1];
     q.tri = true;
+    q.sched = B.sched;
     q.epi.alpha = c;
     q.epi.mirror_same = 1;  // A is stored exactly symmetric by the Gram's mirrored stores
     q.epi.nin = 1;
@@ -222,6 +227,7 @@ extern "C" int po_newton_schulz(const void* G, int dtype, long long batch, long 
     u.a[0] = Bop.v[0]; u.a[1] = Bop.v[1];
     u.b[0] = X.v[0]; u.b[1] = X.v[1];
     u.b_kmajor = false;
+    u.sched = B.sched;
     u.epi.alpha = 1.0f;
     u.epi.nin = 1;
     u.epi.in[0] = epi_in(B.xf, IN_F32, B.ldx, xs, a);

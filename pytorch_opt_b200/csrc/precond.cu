@@ -12,6 +12,7 @@ namespace {
 struct PrecondBufs {
   __nv_bfloat16 *lh, *ll, *gh, *gl, *rh, *rl, *ph, *pl;
   long long ldl, ldg, ldr;
+  unsigned int* sched;  // tile queue of the two products
 };
 
 void precond_layout(Arena& ar, long long m, long long n, bool split, PrecondBufs& B) {
@@ -27,6 +28,7 @@ void precond_layout(Arena& ar, long long m, long long n, bool split, PrecondBufs
   B.gl = split ? take(m * B.ldg) : nullptr;
   B.rl = split ? take(n * B.ldr) : nullptr;
   B.pl = split ? take(m * B.ldg) : nullptr;
+  B.sched = take_sched(ar);
 }
 
 MatView bview(const __nv_bfloat16* p, long long rows, long long cols, long long ld) {
@@ -70,6 +72,7 @@ extern "C" int po_precond_apply(const void* L, long long l_ld, const void* G, lo
   if (workspace == nullptr || ar.overflow()) return set_error(PO_ERR_WORKSPACE, "precond_apply: workspace too small");
 
   int r;
+  if ((r = zero_sched(B.sched, s))) return r;
   AnyMat lm{L, dtype, m, m, l_ld, m * l_ld}, gm{G, dtype, m, n, g_ld, m * g_ld}, rm{R, dtype, n, n, r_ld, n * r_ld};
   if ((r = launch_split_bf16(lm, 1, B.lh, B.ll, B.ldl, m * B.ldl, s))) return r;
   if ((r = launch_split_bf16(gm, 1, B.gh, B.gl, B.ldg, m * B.ldg, s))) return r;
@@ -89,6 +92,7 @@ extern "C" int po_precond_apply(const void* L, long long l_ld, const void* G, lo
     g1.npass = 3;
   }
   g1.b_kmajor = false;
+  g1.sched = B.sched;
   g1.chunked = split && 3 * m > 2048;
   g1.epi.alpha = 1.0f;
   g1.epi.nout = split ? 2 : 1;
@@ -110,6 +114,7 @@ extern "C" int po_precond_apply(const void* L, long long l_ld, const void* G, lo
     g2.npass = 3;
   }
   g2.b_kmajor = false;
+  g2.sched = B.sched;
   g2.chunked = split && 3 * n > 2048;
   g2.epi.alpha = 1.0f;
   g2.epi.nout = 1;

@@ -55,6 +55,7 @@ struct RootBufs {
   Slot X[2], D[2], T[3];
   RootState st;
   long long ld;
+  unsigned int* sched;  // tile queue of the products
 };
 
 constexpr int kTmpSlots = 3;
@@ -82,6 +83,7 @@ void root_layout(Arena& ar, long long batch, long long d, int p, RootBufs& B) {
   B.st.result = static_cast<int*>(ar.take(b * 4));
   B.st.iters = static_cast<int*>(ar.take(b * 4));
   B.st.sums = static_cast<double*>(ar.take(b * 8));
+  B.sched = take_sched(ar);
 }
 
 template <int DT>
@@ -232,6 +234,7 @@ int slot_gemm(const RootBufs& B, long long batch, long long d, const Slot& U, co
   g.passes = B.st.passes;
   g.active = B.st.active;
   g.tri = true;
+  g.sched = B.sched;
   const long long bsw = d * B.ld;
   g.epi.alpha = 1.0f;
   if (c1 != nullptr) g.epi.in[g.epi.nin++] = epi_in(c1->f, IN_F32, B.ld, bsw, beta1);
@@ -290,6 +293,7 @@ extern "C" int po_inverse_root(const void* A, int dtype, long long batch, long l
   int r;
   const int nb = static_cast<int>(batch);
   if ((r = check_cuda(cudaMemsetAsync(B.st.sums, 0, batch * 8, s), "memset"))) return r;
+  if ((r = zero_sched(B.sched, s))) return r;
   root_state_init<<<cdiv(batch, 128), 128, 0, s>>>(B.st, nb);
   dim3 grid(cdiv(d, 32), cdiv(d, 32), nb), block(32, 8);
 #define PO_ROOT_PREP(DT)                                                                                        \

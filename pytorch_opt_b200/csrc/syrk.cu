@@ -81,8 +81,9 @@ int prepare(const void* X, int dt, long long rows, long long cols, long long ld,
 // `gram_of_rows`: product over the columns of X (X X^T, K-major operands);
 // otherwise over its rows (X^T X, MN-major operands).
 int syrk_update(float* F, long long f_ld, const Operand& op, bool gram_of_rows, long long d, long long K,
-                float alpha_acc, float beta, cudaStream_t s) {
+                float alpha_acc, float beta, unsigned int* sched, cudaStream_t s) {
   GemmDesc g;
+  g.sched = sched;
   g.kind = KIND_BF16;
   g.M = g.N = static_cast<int>(d);
   g.K = static_cast<int>(K);
@@ -124,15 +125,19 @@ extern "C" int po_kron_factor_update(float* L, long long l_ld, float* R, long lo
   if (l_ld < m || r_ld < n || g_ld < n) return set_error(PO_ERR_ARG, "kron_factor_update: pitch too small");
   if (m > 0x3fffffff || n > 0x3fffffff) return set_error(PO_ERR_ARG, "kron_factor_update: size too large");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (workspace == nullptr) return set_error(PO_ERR_WORKSPACE, "kron_factor_update: workspace required");
   Arena ar(workspace, workspace_bytes);
+  unsigned int* sched = take_sched(ar);
+  if (ar.overflow()) return set_error(PO_ERR_WORKSPACE, "workspace too small (query its *_workspace_bytes)");
   Operand op;
   int r = prepare(G, g_dtype, m, n, g_ld, ar, op, s);
   if (r) return r;
+  if ((r = zero_sched(sched, s))) return r;
   // beta2 == 1: plain sums (reference adds G G^T without scaling).
   const float keep = beta2 == 1.0 ? 1.0f : static_cast<float>(beta2);
   const float add = beta2 == 1.0 ? 1.0f : static_cast<float>(1.0 - beta2);
-  if ((r = syrk_update(L, l_ld, op, /*gram_of_rows=*/true, m, n, add, keep, s))) return r;
-  return syrk_update(R, r_ld, op, /*gram_of_rows=*/false, n, m, add, keep, s);
+  if ((r = syrk_update(L, l_ld, op, /*gram_of_rows=*/true, m, n, add, keep, sched, s))) return r;
+  return syrk_update(R, r_ld, op, /*gram_of_rows=*/false, n, m, add, keep, sched, s);
 }
 
 extern "C" size_t po_syrk_workspace_bytes(long long rows, long long d, int x_dtype) {
@@ -154,11 +159,15 @@ extern "C" int po_syrk_ema(float* F, long long d, long long f_ld, const void* X,
     if (first) return check_cuda(cudaMemset2DAsync(F, f_ld * 4, 0, d * 4, d, s), "memset");
     return set_error(PO_ERR_UNSUPPORTED, "syrk_ema: EMA with an empty batch");
   }
+  if (workspace == nullptr) return set_error(PO_ERR_WORKSPACE, "syrk_ema: workspace required");
   Arena ar(workspace, workspace_bytes);
+  unsigned int* sched = take_sched(ar);
+  if (ar.overflow()) return set_error(PO_ERR_WORKSPACE, "workspace too small (query its *_workspace_bytes)");
   Operand op;
   int r = prepare(X, x_dtype, rows, d, x_ld, ar, op, s);
   if (r) return r;
+  if ((r = zero_sched(sched, s))) return r;
   const float a = first ? static_cast<float>(alpha) : static_cast<float>((1.0 - beta) * alpha);
   const float b = first ? 0.0f : static_cast<float>(beta);
-  return syrk_update(F, f_ld, op, /*gram_of_rows=*/false, d, rows, a, b, s);
+  return syrk_update(F, f_ld, op, /*gram_of_rows=*/false, d, rows, a, b, sched, s);
 }
