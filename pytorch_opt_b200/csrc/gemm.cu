@@ -236,12 +236,9 @@ int launch_gemm(const GemmDesc& d, cudaStream_t stream) {
   P.tiles_m = cdiv(d.M, tm);
   P.tiles_n = cdiv(d.N, bn);
   P.tri = d.tri ? 1 : 0;
-  // Raster band height and A residency hint; PO_GEMM_GROUP / PO_GEMM_AKEEP in
-  // the environment override them (for measurement).
+  // Raster band height (8 measured best on the Newton-Schulz products:
+  // 4, 16 and 32 all read more from DRAM).
   P.group = 8;
-  P.a_keep = 0;
-  if (const char* e = getenv("PO_GEMM_GROUP")) P.group = atoi(e) > 0 ? atoi(e) : 8;
-  if (const char* e = getenv("PO_GEMM_AKEEP")) P.a_keep = atoi(e) != 0;
   P.tiles_per_batch = d.tri ? P.tiles_m * (P.tiles_m + 1) / 2 : P.tiles_m * P.tiles_n;
   const long long total = static_cast<long long>(P.tiles_per_batch) * d.batch;
   if (total > 0x7fffffffLL) return set_error(PO_ERR_ARG, "launch_gemm: too many tiles");

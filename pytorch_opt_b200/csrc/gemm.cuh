@@ -94,7 +94,6 @@ struct alignas(64) GemmParams {
   int a4d, b4d;  // MN-major operand mapped as 4-D [batch][MN / (128 B)][K][128 B]: one TMA copy per stage
   int group;     // row tiles per raster band (tiles of a band share A panels through L2)
   unsigned int* sched;  // {next tile, CTAs finished}: dynamic tile queue (two-SM kernel), null = static
-  int a_keep;    // load A with the L2 evict-last policy (its panels are re-read across the band)
   const int* active;  // per batch: nonzero = compute (nullable: all)
   const int* passes;  // per batch pass count (nullable: npass)
   int* err;           // device error word
@@ -521,7 +520,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------ TMA producer
-      const uint64_t keep = policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -544,11 +542,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
           uint8_t* sa = tiles + stage * C::STAGE_BYTES;
           uint8_t* sb = sa + C::A_BYTES;
           if (!A_MN) {
-            if (P.a_keep) tma_load_3d_hint(sa, ma, full + stage, k0, tc.mt * BM, tc.b, keep);
-            else tma_load_3d(sa, ma, full + stage, k0, tc.mt * BM, tc.b);
+            tma_load_3d(sa, ma, full + stage, k0, tc.mt * BM, tc.b);
           } else if (P.a4d) {
-            if (P.a_keep) tma_load_4d_hint(sa, ma, full + stage, 0, k0, tc.mt * BM / (128 / C::ES), tc.b, keep);
-            else tma_load_4d(sa, ma, full + stage, 0, k0, tc.mt * BM / (128 / C::ES), tc.b);
+            tma_load_4d(sa, ma, full + stage, 0, k0, tc.mt * BM / (128 / C::ES), tc.b);
           } else {
 #pragma unroll
             for (int i = 0; i < BM * C::ES / 128; ++i)

@@ -120,7 +120,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------ TMA producer (both CTAs)
-      const uint64_t keep = policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -165,11 +164,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
           uint8_t* sa = tiles + stage * C::STAGE_BYTES;
           uint8_t* sb = sa + C::A_BYTES;
           if (!A_MN) {
-            if (P.a_keep) tma_load_3d_pair_hint(sa, ma, bar, k0, arow, tc.b, keep);
-            else tma_load_3d_pair(sa, ma, bar, k0, arow, tc.b);
+            tma_load_3d_pair(sa, ma, bar, k0, arow, tc.b);
           } else if (P.a4d) {
-            if (P.a_keep) tma_load_4d_pair_hint(sa, ma, bar, 0, k0, arow / (128 / C::ES), tc.b, keep);
-            else tma_load_4d_pair(sa, ma, bar, 0, k0, arow / (128 / C::ES), tc.b);
+            tma_load_4d_pair(sa, ma, bar, 0, k0, arow / (128 / C::ES), tc.b);
           } else {
 #pragma unroll
             for (int i = 0; i < 128 * C::ES / 128; ++i)
