@@ -40,6 +40,14 @@ METRIC = "Muon NS5 step ms (8B shapes)"
 MEASURED_PEAKS = os.path.join(HERE, "MEASURED_PEAKS.json")
 
 
+
+# DRAM traffic (ncu dram__bytes_read.sum + dram__bytes_write.sum, summed over
+# the Newton-Schulz product launches) of the two captured workloads; the
+# commands and per-kernel figures are in profiles/launches_llama8b_muon_step.md
+# and profiles/tc_gemm_pair_ns4096.md.
+LLAMA_STEP_TRAFFIC = 1_160_370_000_000   # bytes per 1-GPU step (823.4 GB read + 337.0 GB write)
+NS4096_CALL_TRAFFIC = 14_080_000_000     # bytes per NS5 call on 4 x 4096^2 (9.50 GB read + 4.58 GB write)
+
 def llama_shapes():
     return LLAMA_LAYER * 32
 
@@ -286,9 +294,14 @@ def run_ours(args, rank, world, local_rank):
                        "l2": "inputs larger than L2 (13.96 GB of bf16 params and grads per step)",
                        "algorithmic_tflop_per_step": round(total_flops / 1e12, 1)},
             "tflops": round(total_flops / (step_ms * 1e-3) / 1e12, 1),
-            "roofline": {"bound": "tensor", "kernel": "tc_gemm_kernel (Newton-Schulz products)",
+            "roofline": {"bound": "tensor",
+                         "kernel": "tc_gemm_pair_kernel (Newton-Schulz products, 256x256 tiles on SM pairs)",
                          "achieved": round(gemm_tflops, 1), "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
-                         "frac": round(gemm_tflops / pk["bf16_sustained"], 3), "traffic": None,
+                         "frac": round(gemm_tflops / pk["bf16_sustained"], 3),
+                         "traffic": LLAMA_STEP_TRAFFIC if world == 1 else None,
+                         "traffic_unit": "DRAM bytes per step of all Newton-Schulz product launches (ncu "
+                                         "dram__bytes_read.sum + dram__bytes_write.sum; 1 GPU only, "
+                                         "profiles/launches_llama8b_muon_step.md)",
                          "peak_source": pk["source"] + " bf16 sustained (MEASURED_PEAKS.json)",
                          "peak_bf16_tf32_mix": round(mix_peak, 1),
                          "frac_of_mix": round(gemm_tflops / mix_peak, 3),
@@ -328,15 +341,15 @@ def _timed(fn, steps, warmup, dev, flush=None):
     return sum(a.elapsed_time(b) for a, b in pairs) / steps, clk
 
 
-def _line(args, metric, value, unit, hib, workload, tflops, clk, launches, cpu, extra=None):
+def _line(args, metric, value, unit, hib, workload, tflops, clk, launches, cpu, extra=None, traffic=None):
     pk = peaks()
     line = {"metric": metric, "value": round(value, 4), "unit": unit, "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": None, "higher_is_better": hib, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": workload, "l2": "flushed between timed calls (256 MiB write)"},
-            "roofline": {"bound": "tensor", "kernel": "tc_gemm_kernel", "achieved": round(tflops, 1),
+            "roofline": {"bound": "tensor", "kernel": "tc_gemm_pair_kernel", "achieved": round(tflops, 1),
                          "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
-                         "frac": round(tflops / pk["bf16_sustained"], 3), "traffic": None,
+                         "frac": round(tflops / pk["bf16_sustained"], 3), "traffic": traffic,
                          "peak_source": pk["source"] + " bf16 sustained (MEASURED_PEAKS.json)",
                          "how": "dense algorithmic FLOPs of the call / its CUDA-event time"},
             "clocks": clk, "gpu_launches": launches, "e2e": None, "cpu_baseline": cpu}
@@ -391,7 +404,8 @@ def run_secondary(args, rank):
         m = min(G.shape[-2:])
         launches = 2 + 3 * 5
         _line(args, f"{'NS5 768x3072' if w == 'ns768' else 'NS5 4x4096^2'} ms", ms, "ms", False, desc,
-              fl / (ms * 1e-3) / 1e12, clk, launches * args.steps, cpu, {"ms_per_step": round(ms, 4)})
+              fl / (ms * 1e-3) / 1e12, clk, launches * args.steps, cpu, {"ms_per_step": round(ms, 4)},
+              traffic=NS4096_CALL_TRAFFIC if w == "ns4096" else None)
         return 0
     if w == "gpt2":        # config 2
         shapes = [(768, 2304), (768, 768), (768, 3072), (3072, 768)]

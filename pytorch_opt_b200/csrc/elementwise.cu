@@ -80,52 +80,93 @@ int launch_sumsq(const AnyMat& M, int batch, double* sums, cudaStream_t s) {
 }
 
 // --------------------------------------------------------------- ns_pack
-// One 32x32 output tile per block (32 x 8 threads). Output element (r, c)
-// comes from src(c, r) when TRANS.
+// One 32 x 128 output tile per block (256 threads): each thread writes four
+// consecutive columns of a row with 16-byte (fp32) / 8-byte (bf16) stores.
+// Output element (r, c) comes from src(c, r) when TRANS, staged through a
+// shared-memory tile read along src rows.
+constexpr int kPackRows = 32, kPackCols = 128;
+
+__device__ __forceinline__ void pack_store4(float* xf, void* xop, void* xlo, int op_kind, long long o, int nvalid,
+                                            bool vec, const float (&v)[4]) {
+  if (vec && nvalid == 4) {
+    *reinterpret_cast<float4*>(xf + o) = make_float4(v[0], v[1], v[2], v[3]);
+    if (op_kind == OUT_BF16) {
+      __nv_bfloat162 h[2] = {__floats2bfloat162_rn(v[0], v[1]), __floats2bfloat162_rn(v[2], v[3])};
+      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(xop) + o) = *reinterpret_cast<const uint2*>(h);
+      if (xlo != nullptr) {
+        const float2 f0 = __bfloat1622float2(h[0]), f1 = __bfloat1622float2(h[1]);
+        __nv_bfloat162 l[2] = {__floats2bfloat162_rn(v[0] - f0.x, v[1] - f0.y),
+                               __floats2bfloat162_rn(v[2] - f1.x, v[3] - f1.y)};
+        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(xlo) + o) = *reinterpret_cast<const uint2*>(l);
+      }
+    } else {
+      *reinterpret_cast<float4*>(static_cast<float*>(xop) + o) =
+          make_float4(round_tf32(v[0]), round_tf32(v[1]), round_tf32(v[2]), round_tf32(v[3]));
+    }
+    return;
+  }
+  for (int j = 0; j < nvalid; ++j) {
+    xf[o + j] = v[j];
+    if (op_kind == OUT_BF16) {
+      const __nv_bfloat16 h = __float2bfloat16_rn(v[j]);
+      static_cast<__nv_bfloat16*>(xop)[o + j] = h;
+      if (xlo != nullptr) static_cast<__nv_bfloat16*>(xlo)[o + j] = __float2bfloat16_rn(v[j] - __bfloat162float(h));
+    } else {
+      static_cast<float*>(xop)[o + j] = round_tf32(v[j]);
+    }
+  }
+}
+
 template <int DT, bool TRANS>
-__global__ void ns_pack_kernel(AnyMat src, const double* sums, float eps, float* xf, void* xop, void* xlo,
-                               int op_kind, long long ldx, long long rows_out, long long cols_out) {
-  __shared__ float tile[32][33];
+__global__ void __launch_bounds__(256) ns_pack_kernel(AnyMat src, const double* sums, float eps, float* xf, void* xop,
+                                                      void* xlo, int op_kind, long long ldx, long long rows_out,
+                                                      long long cols_out, int vec) {
+  __shared__ float tile[TRANS ? kPackCols : 1][kPackRows + 1];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int b = blockIdx.z;
-  const long long r0 = static_cast<long long>(blockIdx.y) * 32, c0 = static_cast<long long>(blockIdx.x) * 32;
+  const long long r0 = static_cast<long long>(blockIdx.y) * kPackRows, c0 = static_cast<long long>(blockIdx.x) * kPackCols;
   const float den = static_cast<float>(sqrt(sums[b])) + eps;
   const long long sbase = b * src.bstride;
   if (TRANS) {
-    // src rows = output columns: read src(c0 + i, r0 + threadIdx.x) coalesced along r.
-    for (int i = threadIdx.y; i < 32; i += 8) {
-      const long long sr = c0 + i, sc = r0 + threadIdx.x;
+    // src rows c0.. (= output columns), src columns r0 + tx: coalesced along the src row.
+    for (int i = ty; i < kPackCols; i += 8) {
+      const long long sr = c0 + i, sc = r0 + tx;
       float v = 0.0f;
       if (sr < cols_out && sc < rows_out) v = static_cast<float>(Elem<DT>::ld(src.ptr, sbase + sr * src.ld + sc));
-      tile[i][threadIdx.x] = v;
+      tile[i][tx] = v;
     }
     __syncthreads();
   }
   const long long xbase = b * rows_out * ldx;
-  for (int i = threadIdx.y; i < 32; i += 8) {
-    const long long r = r0 + i, c = c0 + threadIdx.x;
-    if (r >= rows_out || c >= cols_out) continue;
-    float v = TRANS ? tile[threadIdx.x][i] : static_cast<float>(Elem<DT>::ld(src.ptr, sbase + r * src.ld + c));
-    v = __fdiv_rn(v, den);
-    const long long o = xbase + r * ldx + c;
-    xf[o] = v;
-    if (op_kind == OUT_BF16) {
-      const __nv_bfloat16 h = __float2bfloat16_rn(v);
-      static_cast<__nv_bfloat16*>(xop)[o] = h;
-      if (xlo != nullptr) static_cast<__nv_bfloat16*>(xlo)[o] = __float2bfloat16_rn(v - __bfloat162float(h));
-    } else {
-      static_cast<float*>(xop)[o] = round_tf32(v);
+  const long long c = c0 + 4 * tx;
+  const int nvalid = c >= cols_out ? 0 : static_cast<int>(cols_out - c < 4 ? cols_out - c : 4);
+  for (int i = ty; i < kPackRows; i += 8) {
+    const long long r = r0 + i;
+    if (r >= rows_out || nvalid == 0) continue;
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float x = 0.0f;
+      if (j < nvalid)
+        x = TRANS ? tile[4 * tx + j][i] : static_cast<float>(Elem<DT>::ld(src.ptr, sbase + r * src.ld + c + j));
+      v[j] = __fdiv_rn(x, den);
     }
+    pack_store4(xf, xop, xlo, op_kind, xbase + r * ldx + c, nvalid, vec != 0, v);
   }
 }
 
 template <int DT>
 static void ns_pack_dt(const AnyMat& src, int batch, bool trans, const double* sums, float eps, float* xf, void* xop,
                        void* xlo, int op_kind, long long ldx, long long rows_out, long long cols_out, cudaStream_t s) {
-  dim3 grid(cdiv(cols_out, 32), cdiv(rows_out, 32), batch), block(32, 8);
+  dim3 grid(cdiv(cols_out, kPackCols), cdiv(rows_out, kPackRows), batch);
+  // Vector stores need 16-byte aligned rows of every destination.
+  const uintptr_t bases = reinterpret_cast<uintptr_t>(xf) | reinterpret_cast<uintptr_t>(xop) |
+                          reinterpret_cast<uintptr_t>(xlo);
+  const int vec = (bases & 15) == 0 && ldx % 4 == 0;
   if (trans)
-    ns_pack_kernel<DT, true><<<grid, block, 0, s>>>(src, sums, eps, xf, xop, xlo, op_kind, ldx, rows_out, cols_out);
+    ns_pack_kernel<DT, true><<<grid, 256, 0, s>>>(src, sums, eps, xf, xop, xlo, op_kind, ldx, rows_out, cols_out, vec);
   else
-    ns_pack_kernel<DT, false><<<grid, block, 0, s>>>(src, sums, eps, xf, xop, xlo, op_kind, ldx, rows_out, cols_out);
+    ns_pack_kernel<DT, false><<<grid, 256, 0, s>>>(src, sums, eps, xf, xop, xlo, op_kind, ldx, rows_out, cols_out, vec);
 }
 
 int launch_ns_pack(const AnyMat& src, int batch, bool trans, const double* sums, float eps, float* xf, void* xop,
