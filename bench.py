@@ -407,6 +407,37 @@ def run_secondary(args, rank):
               fl / (ms * 1e-3) / 1e12, clk, launches * args.steps, cpu, {"ms_per_step": round(ms, 4)},
               traffic=NS4096_CALL_TRAFFIC if w == "ns4096" else None)
         return 0
+    if w == "gemm":        # the product kernel alone, beside cuBLAS on the same shape
+        import ctypes
+        from pytorch_opt_b200 import _lib
+        lib = _lib.load()
+        M, N, K = args.gemm
+        bf16 = args.gemm_dtype == "bf16"
+        dt = torch.bfloat16 if bf16 else torch.float32
+        g = torch.Generator(device="cpu").manual_seed(5)
+        A = torch.randn(M, K, generator=g).to(dev, dt)
+        Bt = torch.randn(N, K, generator=g).to(dev, dt)     # B stored [N][K]: both operands K-major
+        C = torch.zeros(M, N, device=dev)
+        code = 1 if bf16 else 0
+        nb = lib.po_matmul_workspace_bytes(1, M, N, K, code, 0)
+        ws = _lib.workspace(nb, dev)
+        stream = _lib.stream_ptr(dev)
+
+        def call():
+            _lib.check(lib.po_matmul(A.data_ptr(), K, M * K, 0, Bt.data_ptr(), K, N * K, 1,
+                                     ctypes.c_void_p(C.data_ptr()), N, M * N, code, 0, 1, M, N, K, 1.0, 0.0,
+                                     ws.data_ptr(), nb, stream), "po_matmul")
+        ms, clk = _timed(call, args.steps, args.warmup, dev, flush)
+        torch.backends.cuda.matmul.allow_tf32 = True
+        ms_lib, _ = _timed(lambda: torch.matmul(A, Bt.t()), args.steps, args.warmup, dev, flush)
+        fl = 2.0 * M * N * K
+        _line(args, f"GEMM {M}x{N}x{K} {args.gemm_dtype} TFLOP/s", fl / (ms * 1e-3) / 1e12, "TFLOP/s", True,
+              f"po_matmul, K-major A and B, fp32 C, {args.gemm_dtype} tensor-core operands",
+              fl / (ms * 1e-3) / 1e12, clk, args.steps, None,
+              {"ms_per_step": round(ms, 4),
+               "library_comparison": {"torch.matmul (cuBLAS) TFLOP/s": round(fl / (ms_lib * 1e-3) / 1e12, 1),
+                                      "note": "cuBLAS writes a bf16/fp32 C of the operand type"}})
+        return 0
     if w == "gpt2":        # config 2
         shapes = [(768, 2304), (768, 768), (768, 3072), (3072, 768)]
         groups, k = [], 0
@@ -518,9 +549,13 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="llama8b", choices=("llama8b", "ns768", "ns4096", "gpt2", "shampoo", "kfac"),
-                    help="llama8b (default, config 5); the others are single-GPU measurements of configs 1-4 "
-                         "and the 4x4096^2 profiling case")
+    ap.add_argument("--workload", default="llama8b",
+                    choices=("llama8b", "ns768", "ns4096", "gpt2", "shampoo", "kfac", "gemm"),
+                    help="llama8b (default, config 5); the others are single-GPU measurements of configs 1-4, "
+                         "the 4x4096^2 profiling case and the bare product kernel (gemm)")
+    ap.add_argument("--gemm", type=int, nargs=3, default=(8192, 8192, 8192), metavar=("M", "N", "K"),
+                    help="shape of --workload gemm")
+    ap.add_argument("--gemm-dtype", choices=("bf16", "tf32"), default="bf16")
     args = ap.parse_args(argv)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
