@@ -170,6 +170,51 @@ class ShardedMuon:
         self.local_step(ns_events)
         self.exchange()
 
+    def step_from_host(self, host_slot: torch.Tensor, ns_events: list | None = None) -> None:
+        """One step whose gradients arrive from host memory.
+
+        ``host_slot``: this rank's gradient slot (``layout.slot`` elements of
+        the gradient dtype), ideally in pinned memory. Each shape group's
+        gradients are copied on a side stream, smallest group first, and the
+        group is stepped as soon as its copy lands, so the copies of the later
+        groups overlap the Newton–Schulz work of the earlier ones; only the
+        first (smallest) copy is exposed. Results are identical to copying the
+        whole slot and calling ``step``.
+        """
+        if host_slot.numel() < self.layout.slot:
+            raise ValueError(f"host_slot holds {host_slot.numel()} elements, the slot needs {self.layout.slot}")
+        groups = self.layout.groups[self.rank]
+
+        def host_view(k):
+            g = groups[k]
+            r, c = g.shape
+            return host_slot[g.offset:g.offset + len(g.indices) * r * c].view(len(g.indices), r, c)
+
+        if self.compute is not None:  # host-side (gloo) path: no streams
+            for k, (_, grad) in enumerate(self.groups):
+                grad.copy_(host_view(k))
+            self.step(ns_events)
+            return
+        dev = self.params_flat.device
+        main = torch.cuda.current_stream(dev)
+        if getattr(self, "_copy_stream", None) is None:
+            self._copy_stream = torch.cuda.Stream(dev)
+        cs = self._copy_stream
+        order = sorted(range(len(self.groups)), key=lambda k: (self.groups[k].grads.numel(), k))
+        cs.wait_stream(main)  # the previous step has finished reading the gradient buffers
+        landed = []
+        with torch.cuda.stream(cs):
+            for k in order:
+                self.groups[k].grads.copy_(host_view(k), non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(cs)
+                landed.append(ev)
+        self._sq.zero_()
+        for k, ev in zip(order, landed):
+            main.wait_event(ev)
+            muon_group_step(self.groups[k], sq_sum=self._sq[k], workspace=self._ws, ns_events=ns_events, **self.hp)
+        self.exchange()
+
     def launches_per_step(self) -> int:
         """Kernels this library launches per local step (the all-gather is NCCL's)."""
         total = 0

@@ -329,3 +329,29 @@ def test_grouped_muon_vs_oracle_gpt2_shapes(cuda):
             p1 = O.bf16_round(_np(p0[b]) * np.float32(1.0 - 0.02 * 0.01))
             p2 = O.bf16_round(p1 + O.bf16_round(np.float32(-0.02 * O.muon_scale(shp))) * O_gpu)
             np.testing.assert_array_equal(_np(grp.params[b]), p2)
+
+
+def test_sharded_step_from_host_equals_copy_then_step(cuda):
+    """Per-group host-to-device copies overlapped with the step give the same
+    parameters, bit for bit, as one slot copy followed by the step."""
+    from pytorch_opt_b200.dist import ShardLayout, ShardedMuon
+    shapes = [(768, 2304), (768, 768), (3072, 768), (768, 768), (256, 1024)]
+    lay = ShardLayout(shapes, 1)
+    g = torch.Generator().manual_seed(9)
+    p0 = (torch.randn(lay.numel, generator=g) * 0.02).bfloat16()
+    host = (torch.randn(lay.slot, generator=g) * 0.02).bfloat16().pin_memory()
+    out = []
+    for use_host in (False, True):
+        params = p0.clone().to(cuda)
+        grads = torch.zeros(lay.numel, dtype=torch.bfloat16, device=cuda)
+        sm = ShardedMuon(lay, params, grads, 0, lr=0.02, weight_decay=0.01)
+        for _ in range(2):
+            if use_host:
+                sm.step_from_host(host)
+            else:
+                lay.slot_view(grads, 0).copy_(host)
+                sm.step()
+        torch.cuda.synchronize(cuda)
+        out.append(params.cpu())
+    assert torch.equal(out[0], out[1])
+

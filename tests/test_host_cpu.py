@@ -141,3 +141,31 @@ def test_shard_layout_is_disjoint_and_grouped():
                 assert tuple(v.shape) == (len(g.indices), *g.shape)
                 for k, i in enumerate(g.indices):  # group view k is matrix i
                     assert v[k].data_ptr() == lay.matrix(flat, i).data_ptr()
+
+
+def test_step_from_host_matches_copy_then_step_on_cpu():
+    """The host-gradient step (per-group copies) equals copying the slot and stepping."""
+    from pytorch_opt_b200.dist import ShardedMuon
+    shapes = [(64, 96), (96, 64), (64, 96), (32, 32), (16, 48)]
+    lay = ShardLayout(shapes, 1)
+    g = torch.Generator().manual_seed(3)
+    host = torch.randn(lay.slot, generator=g)
+
+    def fake_update(p, grad):
+        p.add_(grad * 0.5 + 1.0)
+
+    out = []
+    for use_host in (False, True):
+        params = torch.zeros(lay.numel)
+        grads = torch.zeros(lay.numel)
+        sm = ShardedMuon(lay, params, grads, 0, compute=fake_update)
+        if use_host:
+            sm.step_from_host(host)
+        else:
+            lay.slot_view(grads, 0).copy_(host)
+            sm.step()
+        out.append(params.clone())
+    assert torch.equal(out[0], out[1])
+    with pytest.raises(ValueError):
+        ShardedMuon(lay, torch.zeros(lay.numel), torch.zeros(lay.numel), 0, compute=fake_update).step_from_host(
+            host[:-1])
