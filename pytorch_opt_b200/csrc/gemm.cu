@@ -181,6 +181,13 @@ static bool use_pair(const GemmDesc& d, int bn) {
   return cost2 <= cost1;
 }
 
+bool gemm_uses_pair(const GemmDesc& d) {
+  int bn = d.bn;
+  if (bn == 0) bn = (d.tri || d.N <= 128) ? 128 : 256;
+  if (d.tri || d.chunked) bn = 128;
+  return !d.chunked && use_pair(d, bn);
+}
+
 int launch_gemm(const GemmDesc& d, cudaStream_t stream) {
   if (d.M <= 0 || d.N <= 0 || d.batch <= 0) return PO_OK;
   if (d.K <= 0) return set_error(PO_ERR_ARG, "launch_gemm: K must be positive");

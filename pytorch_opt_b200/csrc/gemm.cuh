@@ -56,6 +56,8 @@ struct EpiOut {
   int trans;      // write element (i, j) to ptr[j*ld + i]
   int vec;
   int zero_diag;  // store 0 on the diagonal (operand copies for the diagonal split)
+  int lower_only; // symmetric product: skip the mirrored copy (readers use only lower-triangle
+                  // tiles and whole diagonal tiles of a product tiled the same way)
 };
 
 constexpr int kGemmThreads = 320;                  // 10 warps
@@ -458,7 +460,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCo
     // The full product is symmetric: the mirrored element takes the same value.
 #pragma unroll
     for (int o = 0; o < kMaxEpiOut; ++o)
-      if (o < E.nout) store_col(E.out[o], tc.b, row, col0, N, v);
+      if (o < E.nout && !E.out[o].lower_only) store_col(E.out[o], tc.b, row, col0, N, v);
   }
 }
 

@@ -44,6 +44,8 @@ EpiIn epi_in(const void* ptr, int in_kind, long long ld, long long bstride, floa
 EpiOut epi_out(void* ptr, int out_kind, long long ld, long long bstride, bool trans = false);
 
 int launch_gemm(const GemmDesc& d, cudaStream_t stream);
+// Whether launch_gemm runs this product on the two-SM kernel (256 x 256 tiles).
+bool gemm_uses_pair(const GemmDesc& d);
 
 // Tile-queue words for GemmDesc::sched, carved from an op's workspace.
 inline unsigned int* take_sched(Arena& ar) { return static_cast<unsigned int*>(ar.take(8)); }

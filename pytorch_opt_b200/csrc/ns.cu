@@ -197,7 +197,11 @@ extern "C" int po_newton_schulz(const void* G, int dtype, long long batch, long 
     g.sched = B.sched;
     g.epi.alpha = 1.0f;
     g.epi.mirror_same = 1;
-    g.epi.out[g.epi.nout++] = epi_out(B.af, OUT_F32, B.ldm, ms);
+    // The fp32 A is read only as the square's addend, on the square's own
+    // (identically shaped) lower-triangle and diagonal tiles: no mirrored copy.
+    g.pair = gemm_uses_pair(g) ? 1 : 0;
+    g.epi.out[g.epi.nout] = epi_out(B.af, OUT_F32, B.ldm, ms);
+    g.epi.out[g.epi.nout++].lower_only = 1;
     add_op_outputs(g.epi, pr, a_hi, a_lo, B.ldm, ms);
     if ((r = launch_gemm(g, s))) return r;
 
@@ -209,6 +213,7 @@ extern "C" int po_newton_schulz(const void* G, int dtype, long long batch, long 
     q.a[0] = Aop.v[0]; q.a[1] = Aop.v[1];
     q.b[0] = Aop.v[0]; q.b[1] = Aop.v[1];
     q.tri = true;
+    q.pair = g.pair;  // same tiling as the Gram, whose fp32 A holds only those tiles
     q.sched = B.sched;
     q.epi.alpha = c;
     q.epi.mirror_same = 1;  // A is stored exactly symmetric by the Gram's mirrored stores
