@@ -137,3 +137,37 @@ def test_root_on_pair_tiles(cuda, monkeypatch):
     out = native.inverse_matrix_root(torch.from_numpy(A).to(cuda), 4, 1e-6, "newton", False, 100, 1e-6)
     res = O.root_residual(out.double().cpu().numpy(), A.astype(np.float64), 4, 1e-6)
     assert res <= 1e-4
+
+
+def test_root_batched_mixed_conditioning_on_pair_tiles(cuda, monkeypatch):
+    """Items that converge at different iterations are skipped by later
+    launches (per-item active flags and pass counts) while the other items'
+    tiles keep flowing through the two-SM kernel's dynamic tile queue."""
+    monkeypatch.setenv("PO_GEMM_PAIR", "1")
+    rng = np.random.default_rng(17)
+    d = 600  # ragged: three 256-row tiles, the last one partial
+    mats = []
+    for k, scale in enumerate((1.0, 40.0, 0.0)):
+        if scale == 0.0:
+            mats.append(np.eye(d) * 3.0)  # converges at once
+            continue
+        X = rng.standard_normal((2 * d, d))
+        mats.append(X.T @ X / (2 * d) * scale + 1e-3 * np.eye(d))
+    A = torch.from_numpy(np.stack(mats).astype(np.float32)).to(cuda)
+    out = native.inverse_matrix_root(A, 4, 1e-6, "newton", False, 100, 1e-6)
+    for i, M in enumerate(mats):
+        assert O.root_residual(out[i].double().cpu().numpy(), M.astype(np.float32).astype(np.float64), 4, 1e-6) <= 1e-4
+
+
+@pytest.mark.parametrize("shape", [(3, 640, 1664), (2, 1400, 520)])
+def test_ns_batched_ragged_on_pair_tiles(cuda, monkeypatch, shape):
+    """Batched, ragged and tall (transposed) Newton-Schulz on two-SM tiles."""
+    monkeypatch.setenv("PO_GEMM_PAIR", "1")
+    rng = np.random.default_rng(23)
+    G = rng.standard_normal(shape).astype(np.float32)
+    got = native.newton_schulz_orthogonalize(torch.from_numpy(G).to(cuda), 5, 3.4445, -4.7750, 2.0315, 1e-7)
+    for b in range(shape[0]):
+        want = O.newton_schulz(G[b], 5, (3.4445, -4.7750, 2.0315), 1e-7)
+        rel = float(np.linalg.norm(got[b].double().cpu().numpy() - want) / np.linalg.norm(want))
+        assert rel <= 1e-2
+
