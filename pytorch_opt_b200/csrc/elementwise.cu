@@ -82,8 +82,6 @@ int launch_sumsq(const AnyMat& M, int batch, double* sums, cudaStream_t s) {
 // --------------------------------------------------------------- ns_pack
 // One 32 x 128 output tile per block (256 threads): each thread writes four
 // consecutive columns of a row with 16-byte (fp32) / 8-byte (bf16) stores.
-// Output element (r, c) comes from src(c, r) when TRANS, staged through a
-// shared-memory tile read along src rows.
 constexpr int kPackRows = 32, kPackCols = 128;
 
 __device__ __forceinline__ void pack_store4(float* xf, void* xop, void* xlo, int op_kind, long long o, int nvalid,
@@ -117,26 +115,15 @@ __device__ __forceinline__ void pack_store4(float* xf, void* xop, void* xlo, int
   }
 }
 
-template <int DT, bool TRANS>
+template <int DT>
 __global__ void __launch_bounds__(256) ns_pack_kernel(AnyMat src, const double* sums, float eps, float* xf, void* xop,
                                                       void* xlo, int op_kind, long long ldx, long long rows_out,
                                                       long long cols_out, int vec) {
-  __shared__ float tile[TRANS ? kPackCols : 1][kPackRows + 1];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int b = blockIdx.z;
   const long long r0 = static_cast<long long>(blockIdx.y) * kPackRows, c0 = static_cast<long long>(blockIdx.x) * kPackCols;
   const float den = static_cast<float>(sqrt(sums[b])) + eps;
   const long long sbase = b * src.bstride;
-  if (TRANS) {
-    // src rows c0.. (= output columns), src columns r0 + tx: coalesced along the src row.
-    for (int i = ty; i < kPackCols; i += 8) {
-      const long long sr = c0 + i, sc = r0 + tx;
-      float v = 0.0f;
-      if (sr < cols_out && sc < rows_out) v = static_cast<float>(Elem<DT>::ld(src.ptr, sbase + sr * src.ld + sc));
-      tile[i][tx] = v;
-    }
-    __syncthreads();
-  }
   const long long xbase = b * rows_out * ldx;
   const long long c = c0 + 4 * tx;
   const int nvalid = c >= cols_out ? 0 : static_cast<int>(cols_out - c < 4 ? cols_out - c : 4);
@@ -145,28 +132,81 @@ __global__ void __launch_bounds__(256) ns_pack_kernel(AnyMat src, const double* 
     if (r >= rows_out || nvalid == 0) continue;
     float v[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float x = 0.0f;
-      if (j < nvalid)
-        x = TRANS ? tile[4 * tx + j][i] : static_cast<float>(Elem<DT>::ld(src.ptr, sbase + r * src.ld + c + j));
-      v[j] = __fdiv_rn(x, den);
-    }
+    for (int j = 0; j < 4; ++j)
+      v[j] = __fdiv_rn(j < nvalid ? static_cast<float>(Elem<DT>::ld(src.ptr, sbase + r * src.ld + c + j)) : 0.0f, den);
     pack_store4(xf, xop, xlo, op_kind, xbase + r * ldx + c, nvalid, vec != 0, v);
+  }
+}
+
+// Transposing pack: output element (r, c) = src(c, r) / den. 64 x 64 tiles
+// through shared memory; both the src rows read (64 elements) and the output
+// rows written (64 elements, two per lane) are contiguous across a warp.
+constexpr int kPackT = 64;
+
+template <int DT>
+__global__ void __launch_bounds__(256) ns_pack_t_kernel(AnyMat src, const double* sums, float eps, float* xf,
+                                                        void* xop, void* xlo, int op_kind, long long ldx,
+                                                        long long rows_out, long long cols_out, int vec) {
+  __shared__ float tile[kPackT][kPackT + 1];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int b = blockIdx.z;
+  const long long r0 = static_cast<long long>(blockIdx.y) * kPackT, c0 = static_cast<long long>(blockIdx.x) * kPackT;
+  const float den = static_cast<float>(sqrt(sums[b])) + eps;
+  const long long sbase = b * src.bstride;
+  // src rows c0.. (output columns), src columns r0.. (output rows).
+  for (int i = ty; i < kPackT; i += 8) {
+    const long long sr = c0 + i;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const long long sc = r0 + 2 * tx + j;
+      float v = 0.0f;
+      if (sr < cols_out && sc < rows_out) v = static_cast<float>(Elem<DT>::ld(src.ptr, sbase + sr * src.ld + sc));
+      tile[i][2 * tx + j] = v;
+    }
+  }
+  __syncthreads();
+  const long long xbase = b * rows_out * ldx;
+  const long long c = c0 + 2 * tx;
+  const int nvalid = c >= cols_out ? 0 : static_cast<int>(cols_out - c < 2 ? cols_out - c : 2);
+  for (int i = ty; i < kPackT; i += 8) {
+    const long long r = r0 + i;
+    if (r >= rows_out || nvalid == 0) continue;
+    const float v0 = __fdiv_rn(tile[2 * tx][i], den), v1 = __fdiv_rn(tile[2 * tx + 1][i], den);
+    const long long o = xbase + r * ldx + c;
+    if (vec && nvalid == 2) {
+      *reinterpret_cast<float2*>(xf + o) = make_float2(v0, v1);
+      if (op_kind == OUT_BF16) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
+        *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(xop) + o) = h;
+        if (xlo != nullptr) {
+          const float2 f = __bfloat1622float2(h);
+          *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(xlo) + o) =
+              __floats2bfloat162_rn(v0 - f.x, v1 - f.y);
+        }
+      } else {
+        *reinterpret_cast<float2*>(static_cast<float*>(xop) + o) = make_float2(round_tf32(v0), round_tf32(v1));
+      }
+    } else {
+      const float vv[4] = {v0, v1, 0.0f, 0.0f};
+      pack_store4(xf, xop, xlo, op_kind, o, nvalid, false, vv);
+    }
   }
 }
 
 template <int DT>
 static void ns_pack_dt(const AnyMat& src, int batch, bool trans, const double* sums, float eps, float* xf, void* xop,
                        void* xlo, int op_kind, long long ldx, long long rows_out, long long cols_out, cudaStream_t s) {
-  dim3 grid(cdiv(cols_out, kPackCols), cdiv(rows_out, kPackRows), batch);
   // Vector stores need 16-byte aligned rows of every destination.
   const uintptr_t bases = reinterpret_cast<uintptr_t>(xf) | reinterpret_cast<uintptr_t>(xop) |
                           reinterpret_cast<uintptr_t>(xlo);
   const int vec = (bases & 15) == 0 && ldx % 4 == 0;
-  if (trans)
-    ns_pack_kernel<DT, true><<<grid, 256, 0, s>>>(src, sums, eps, xf, xop, xlo, op_kind, ldx, rows_out, cols_out, vec);
-  else
-    ns_pack_kernel<DT, false><<<grid, 256, 0, s>>>(src, sums, eps, xf, xop, xlo, op_kind, ldx, rows_out, cols_out, vec);
+  if (trans) {
+    dim3 grid(cdiv(cols_out, kPackT), cdiv(rows_out, kPackT), batch);
+    ns_pack_t_kernel<DT><<<grid, 256, 0, s>>>(src, sums, eps, xf, xop, xlo, op_kind, ldx, rows_out, cols_out, vec);
+  } else {
+    dim3 grid(cdiv(cols_out, kPackCols), cdiv(rows_out, kPackRows), batch);
+    ns_pack_kernel<DT><<<grid, 256, 0, s>>>(src, sums, eps, xf, xop, xlo, op_kind, ldx, rows_out, cols_out, vec);
+  }
 }
 
 int launch_ns_pack(const AnyMat& src, int batch, bool trans, const double* sums, float eps, float* xf, void* xop,
