@@ -200,7 +200,7 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     shapes = llama_shapes()
-    layout = ShardLayout(shapes, world)
+    layout = ShardLayout(shapes, world, chunks=args.exchange_chunks)
     params = torch.zeros(layout.numel, dtype=torch.bfloat16, device=dev)
     grads = torch.zeros(layout.numel, dtype=torch.bfloat16, device=dev)
     for i in range(len(shapes)):
@@ -249,7 +249,7 @@ def run_ours(args, rank, world, local_rank):
     e2e = None
     if not args.no_e2e:
         host = torch.empty(layout.slot, dtype=torch.bfloat16, pin_memory=True)
-        host.copy_(layout.slot_view(grads, rank))
+        host.copy_(layout.slot_tensor(grads, rank))
         sq = torch.zeros(1, dtype=torch.float64, device=dev)
         for _ in range(min(args.warmup, 1)):
             sm.step_from_host(host)
@@ -266,7 +266,7 @@ def run_ours(args, rank, world, local_rank):
         a1.record(stream)
         barrier()
         e2e = {"value": round(max_over_ranks(a0.elapsed_time(a1) / args.steps), 3), "unit": "ms",
-               "h2d_bytes_per_step": int(layout.slot * 2), "d2h_bytes_per_step": 8,
+               "h2d_bytes_per_step": int(layout.slot_elements(rank) * 2), "d2h_bytes_per_step": 8,
                "api": "pytorch_opt_b200.dist.ShardedMuon.step_from_host (per-group H2D copies overlapped with "
                       "the grouped Muon kernels, C ABI) + NCCL all-gather"}
 
@@ -289,7 +289,8 @@ def run_ours(args, rank, world, local_rank):
             "precision": "bf16 tensor-core products on NS steps 1-3, tf32 on steps 4-5, fp32 accumulation",
             "config": {"workload": "Muon step over Llama-3-8B matrix params (224 bf16 matrices, 5 NS steps)",
                        "ns_steps": 5, "momentum": 0.95, "nesterov": True,
-                       "parallelism": f"per-matrix FLOP-balanced shard x{world} + NCCL all-gather",
+                       "parallelism": f"per-matrix FLOP-balanced shard x{world} + NCCL all-gather"
+                                      + (f" in {layout.chunks} chunks overlapped with the step" if world > 1 else ""),
                        "l2": "inputs larger than L2 (13.96 GB of bf16 params and grads per step)",
                        "algorithmic_tflop_per_step": round(total_flops / 1e12, 1)},
             "tflops": round(total_flops / (step_ms * 1e-3) / 1e12, 1),
@@ -555,6 +556,8 @@ def main(argv=None) -> int:
     ap.add_argument("--gemm", type=int, nargs=3, default=(8192, 8192, 8192), metavar=("M", "N", "K"),
                     help="shape of --workload gemm")
     ap.add_argument("--gemm-dtype", choices=("bf16", "tf32"), default="bf16")
+    ap.add_argument("--exchange-chunks", type=int, default=None,
+                    help="all-gather chunks per step for N > 1 (default 4; 1 = one all-gather after the local step)")
     args = ap.parse_args(argv)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -7,13 +7,16 @@ Here every matrix is an independent unit of work:
 
 * ``lpt_assign`` gives each rank a set of matrices by greedy longest-
   processing-time over their Newton–Schulz FLOPs;
-* ``ShardLayout`` places the parameters in one flat buffer of
-  ``world * slot`` elements, rank r's matrices packed (grouped by shape) in
-  slot r, so that every shape group is one ``[count, rows, cols]`` view;
-* ``ShardedMuon.step`` updates the local slot with the grouped kernels and
-  then runs one ``all_gather_into_tensor`` whose output is the parameter
-  buffer itself (in place: the local slot is the input), so after the step
-  every rank holds every updated matrix. Nothing else crosses GPUs.
+* ``ShardLayout`` places the parameters in one flat buffer: each rank's
+  matrices are cut into a few exchange chunks (runs of about equal FLOPs)
+  and grouped by shape inside a chunk, so that every shape group is one
+  ``[count, rows, cols]`` view, and the buffer is ``[chunk][rank][len]``;
+* ``ShardedMuon.step`` updates the local matrices chunk by chunk with the
+  grouped kernels and starts each chunk's ``all_gather_into_tensor`` (in
+  place: the rank's chunk part is the input, the chunk's slice of the buffer
+  the output) as soon as that chunk is stepped, so the exchange of chunk c
+  overlaps the Newton–Schulz work of the later chunks. After the step every
+  rank holds every updated matrix. Nothing else crosses GPUs.
 
 The same code runs over ``gloo`` on CPU tensors for the host-side tests
 (``compute`` can be replaced there, as the kernels need a GPU).
@@ -58,39 +61,81 @@ def lpt_assign(costs: list[float], world: int) -> list[list[int]]:
 class _Group:
     shape: tuple[int, int]
     indices: list[int]  # global matrix indices, in slot order
-    offset: int         # element offset of the group inside its rank's slot
+    offset: int         # element offset of the group inside its rank's slot (chunk after chunk)
+    chunk: int = 0      # exchange chunk the group belongs to
+    flat: int = 0       # element offset of the group in the flat buffer
 
 
 class ShardLayout:
-    """Placement of matrices in a flat ``[world * slot]`` buffer (slot r = rank r's matrices)."""
+    """Placement of matrices in a flat parameter buffer, sharded by rank and chunk.
 
-    def __init__(self, shapes: list[tuple[int, int]], world: int, steps: int = 5, align: int = 64):
+    Each rank's matrices (LPT plan) are cut, in processing order, into
+    ``chunks`` runs of about equal Newton–Schulz FLOPs; inside a run they are
+    grouped by shape. The flat buffer is ``[chunk][world][chunk_len[chunk]]``:
+    chunk c of every rank sits side by side, so chunk c's exchange is one
+    ``all_gather_into_tensor`` whose output is a contiguous slice of the
+    buffer, and it can start as soon as every rank has stepped its chunk c
+    while the later chunks are still being computed. A rank's *slot* is its
+    ``slot = sum(chunk_len)`` elements, chunk after chunk (the layout of
+    host-side gradient slots).
+    """
+
+    def __init__(self, shapes: list[tuple[int, int]], world: int, steps: int = 5, align: int = 64,
+                 chunks: int | None = None):
         self.shapes = [tuple(s) for s in shapes]
         self.world = world
-        self.assign = lpt_assign([ns_flops(r, c, steps) for r, c in self.shapes], world)
+        costs = [ns_flops(r, c, steps) for r, c in self.shapes]
+        self.assign = lpt_assign(costs, world)
+        if chunks is None:
+            chunks = 1 if world == 1 else 4
+        self.chunks = max(1, int(chunks))
+        # Per rank: matrices in processing order (largest shapes first), cut into chunk runs.
+        runs: list[list[list[int]]] = []
+        for r in range(world):
+            mine = sorted(self.assign[r], key=lambda i: (-self.shapes[i][0] * self.shapes[i][1], self.shapes[i], i))
+            total = sum(costs[i] for i in mine)
+            parts: list[list[int]] = [[] for _ in range(self.chunks)]
+            acc = 0.0
+            for i in mine:
+                c = min(self.chunks - 1, int(acc * self.chunks / total)) if total > 0 else 0
+                parts[c].append(i)
+                acc += costs[i]
+            runs.append(parts)
+        # Chunk lengths (max over ranks), then absolute placement.
+        local: list[list[list[tuple]]] = [[[] for _ in range(self.chunks)] for _ in range(world)]
+        self.chunk_len = [align] * self.chunks
+        for r in range(world):
+            for c in range(self.chunks):
+                by_shape: dict[tuple[int, int], list[int]] = {}
+                for i in runs[r][c]:
+                    by_shape.setdefault(self.shapes[i], []).append(i)
+                off = 0
+                for shape in sorted(by_shape, key=lambda sh: (-sh[0] * sh[1], sh)):
+                    idx = sorted(by_shape[shape])
+                    local[r][c].append((shape, idx, off))
+                    off += len(idx) * shape[0] * shape[1]
+                    off = (off + align - 1) // align * align
+                self.chunk_len[c] = max(self.chunk_len[c], off)
+        self.chunk_base = []
+        base = 0
+        for c in range(self.chunks):
+            self.chunk_base.append(base)
+            base += world * self.chunk_len[c]
+        self.slot = sum(self.chunk_len)
         self.groups: list[list[_Group]] = []
         self.offset_of: dict[int, tuple[int, int]] = {}  # matrix -> (rank, element offset in the flat buffer)
-        slot = 0
-        per_rank = []
         for r in range(world):
-            by_shape: dict[tuple[int, int], list[int]] = {}
-            for i in sorted(self.assign[r]):
-                by_shape.setdefault(self.shapes[i], []).append(i)
-            groups, off = [], 0
-            for shape in sorted(by_shape, key=lambda s: (-s[0] * s[1], s)):
-                idx = by_shape[shape]
-                groups.append(_Group(shape, idx, off))
-                off += len(idx) * shape[0] * shape[1]
-                off = (off + align - 1) // align * align
-            per_rank.append((groups, off))
-            slot = max(slot, off)
-        self.slot = max(slot, align)
-        for r, (groups, _) in enumerate(per_rank):
+            groups = []
+            slot_base = 0
+            for c in range(self.chunks):
+                for shape, idx, off in local[r][c]:
+                    flat = self.chunk_base[c] + r * self.chunk_len[c] + off
+                    groups.append(_Group(shape, idx, slot_base + off, c, flat))
+                    n = shape[0] * shape[1]
+                    for k, i in enumerate(idx):
+                        self.offset_of[i] = (r, flat + k * n)
+                slot_base += self.chunk_len[c]
             self.groups.append(groups)
-            for g in groups:
-                n = g.shape[0] * g.shape[1]
-                for k, i in enumerate(g.indices):
-                    self.offset_of[i] = (r, r * self.slot + g.offset + k * n)
 
     @property
     def numel(self) -> int:
@@ -104,16 +149,38 @@ class ShardLayout:
 
     def group_views(self, flat: torch.Tensor, rank: int) -> list[torch.Tensor]:
         """``[count, rows, cols]`` views of rank's shape groups inside ``flat`` (full buffer)."""
-        base = rank * self.slot
         out = []
         for g in self.groups[rank]:
             r, c = g.shape
             n = len(g.indices) * r * c
-            out.append(flat[base + g.offset: base + g.offset + n].view(len(g.indices), r, c))
+            out.append(flat[g.flat:g.flat + n].view(len(g.indices), r, c))
         return out
 
-    def slot_view(self, flat: torch.Tensor, rank: int) -> torch.Tensor:
-        return flat[rank * self.slot:(rank + 1) * self.slot]
+    def chunk_part(self, flat: torch.Tensor, rank: int, chunk: int) -> torch.Tensor:
+        """Rank's part of one exchange chunk (the all-gather input)."""
+        start = self.chunk_base[chunk] + rank * self.chunk_len[chunk]
+        return flat[start:start + self.chunk_len[chunk]]
+
+    def chunk_all(self, flat: torch.Tensor, chunk: int) -> torch.Tensor:
+        """All ranks' parts of one exchange chunk (the all-gather output)."""
+        start = self.chunk_base[chunk]
+        return flat[start:start + self.world * self.chunk_len[chunk]]
+
+    def slot_tensor(self, flat: torch.Tensor, rank: int) -> torch.Tensor:
+        """Copy of rank's slot (its chunk parts, in chunk order)."""
+        return torch.cat([self.chunk_part(flat, rank, c) for c in range(self.chunks)])
+
+    def load_slot(self, flat: torch.Tensor, rank: int, src: torch.Tensor) -> None:
+        """Write a slot-shaped tensor into rank's chunk parts of ``flat``."""
+        off = 0
+        for c in range(self.chunks):
+            n = self.chunk_len[c]
+            self.chunk_part(flat, rank, c).copy_(src[off:off + n], non_blocking=True)
+            off += n
+
+    def slot_elements(self, rank: int) -> int:
+        """Matrix elements (padding excluded) of rank's slot."""
+        return sum(len(g.indices) * g.shape[0] * g.shape[1] for g in self.groups[rank])
 
     def flops(self, rank: int, steps: int = 5) -> float:
         return sum(ns_flops(*self.shapes[i], steps) for i in self.assign[rank])
@@ -149,37 +216,63 @@ class ShardedMuon:
             need = max(ns_workspace_bytes(*g.params.shape) for g in self.groups)
             self._ws = torch.empty(need, dtype=torch.uint8, device=params_flat.device)
 
+    def _step_group(self, k: int, ns_events: list | None) -> None:
+        if self.compute is not None:
+            p, g = self.groups[k]
+            self.compute(p, g)
+        else:
+            muon_group_step(self.groups[k], sq_sum=self._sq[k], workspace=self._ws, ns_events=ns_events, **self.hp)
+
+    def _gather_chunk(self, c: int):
+        """Start chunk c's all-gather (NCCL orders it after the work already queued on the current stream)."""
+        return dist.all_gather_into_tensor(self.layout.chunk_all(self.params_flat, c),
+                                           self.layout.chunk_part(self.params_flat, self.rank, c),
+                                           group=self.pg, async_op=True)
+
+    def _run(self, order_of_chunk, ns_events, before_group=None) -> None:
+        self._sq.zero_()
+        pending = []
+        for c in range(self.layout.chunks):
+            for k in order_of_chunk(c):
+                if before_group is not None:
+                    before_group(k)
+                self._step_group(k, ns_events)
+            if self.layout.world > 1:
+                pending.append(self._gather_chunk(c))
+        for w in pending:
+            w.wait()
+
+    def _chunk_groups(self, c: int) -> list[int]:
+        return [k for k, g in enumerate(self.layout.groups[self.rank]) if g.chunk == c]
+
     def local_step(self, ns_events: list | None = None) -> None:
         """Update this rank's matrices in place (no communication)."""
         self._sq.zero_()
-        if self.compute is not None:
-            for p, g in self.groups:
-                self.compute(p, g)
-            return
-        for i, g in enumerate(self.groups):
-            muon_group_step(g, sq_sum=self._sq[i], workspace=self._ws, ns_events=ns_events, **self.hp)
+        for k in range(len(self.groups)):
+            self._step_group(k, ns_events)
 
     def exchange(self) -> None:
-        """All-gather every rank's updated slot into every rank's parameter buffer."""
+        """All-gather every rank's updated matrices into every rank's parameter buffer."""
         if self.layout.world == 1:
             return
-        local = self.layout.slot_view(self.params_flat, self.rank)
-        dist.all_gather_into_tensor(self.params_flat, local, group=self.pg)
+        for w in [self._gather_chunk(c) for c in range(self.layout.chunks)]:
+            w.wait()
 
     def step(self, ns_events: list | None = None) -> None:
-        self.local_step(ns_events)
-        self.exchange()
+        """Local update and exchange; chunk c's all-gather overlaps the update of chunks c+1.."""
+        self._run(self._chunk_groups, ns_events)
 
     def step_from_host(self, host_slot: torch.Tensor, ns_events: list | None = None) -> None:
         """One step whose gradients arrive from host memory.
 
         ``host_slot``: this rank's gradient slot (``layout.slot`` elements of
-        the gradient dtype), ideally in pinned memory. Each shape group's
-        gradients are copied on a side stream, smallest group first, and the
-        group is stepped as soon as its copy lands, so the copies of the later
-        groups overlap the Newton–Schulz work of the earlier ones; only the
-        first (smallest) copy is exposed. Results are identical to copying the
-        whole slot and calling ``step``.
+        the gradient dtype, chunk after chunk as ``ShardLayout.slot_tensor``
+        lays it out), ideally in pinned memory. Each shape group's gradients
+        are copied on a side stream (within a chunk, smallest group first) and
+        the group is stepped as soon as its copy lands, so the copies overlap
+        the Newton–Schulz work of the groups before them; only the first copy
+        is exposed. Results are identical to copying the slot and calling
+        ``step``.
         """
         if host_slot.numel() < self.layout.slot:
             raise ValueError(f"host_slot holds {host_slot.numel()} elements, the slot needs {self.layout.slot}")
@@ -190,30 +283,32 @@ class ShardedMuon:
             r, c = g.shape
             return host_slot[g.offset:g.offset + len(g.indices) * r * c].view(len(g.indices), r, c)
 
+        def grad_of(k):
+            return self.groups[k][1] if self.compute is not None else self.groups[k].grads
+
+        def order(c):
+            return sorted(self._chunk_groups(c), key=lambda k: (grad_of(k).numel(), k))
+
         if self.compute is not None:  # host-side (gloo) path: no streams
-            for k, (_, grad) in enumerate(self.groups):
-                grad.copy_(host_view(k))
-            self.step(ns_events)
+            for k in range(len(self.groups)):
+                grad_of(k).copy_(host_view(k))
+            self._run(order, ns_events)
             return
         dev = self.params_flat.device
         main = torch.cuda.current_stream(dev)
         if getattr(self, "_copy_stream", None) is None:
             self._copy_stream = torch.cuda.Stream(dev)
         cs = self._copy_stream
-        order = sorted(range(len(self.groups)), key=lambda k: (self.groups[k].grads.numel(), k))
         cs.wait_stream(main)  # the previous step has finished reading the gradient buffers
-        landed = []
+        landed = {}
         with torch.cuda.stream(cs):
-            for k in order:
-                self.groups[k].grads.copy_(host_view(k), non_blocking=True)
-                ev = torch.cuda.Event()
-                ev.record(cs)
-                landed.append(ev)
-        self._sq.zero_()
-        for k, ev in zip(order, landed):
-            main.wait_event(ev)
-            muon_group_step(self.groups[k], sq_sum=self._sq[k], workspace=self._ws, ns_events=ns_events, **self.hp)
-        self.exchange()
+            for c in range(self.layout.chunks):
+                for k in order(c):
+                    grad_of(k).copy_(host_view(k), non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(cs)
+                    landed[k] = ev
+        self._run(order, ns_events, before_group=lambda k: main.wait_event(landed[k]))
 
     def launches_per_step(self) -> int:
         """Kernels this library launches per local step (the all-gather is NCCL's)."""

@@ -49,7 +49,13 @@ def _worker_exchange(rank, world, port, q):
         sm = ShardedMuon(lay, params, grads, rank, compute=fake_update)
         sm.step()
         ok = all(torch.all(lay.matrix(params, i) == float(i + 1)) for i in range(len(SHAPES)))
-        q.put((rank, bool(ok), sum(touched), len(lay.assign[rank])))
+        n_local = sum(touched)
+        # The host-gradient step: the same update again from a slot-shaped copy.
+        host = lay.slot_tensor(grads, rank)
+        grads.zero_()
+        sm.step_from_host(host)
+        ok = ok and all(torch.all(lay.matrix(params, i) == 2.0 * (i + 1)) for i in range(len(SHAPES)))
+        q.put((rank, bool(ok), n_local, len(lay.assign[rank])))
         dist.destroy_process_group()
     except Exception:
         q.put((rank, False, traceback.format_exc(), -1))

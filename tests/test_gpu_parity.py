@@ -349,7 +349,7 @@ def test_sharded_step_from_host_equals_copy_then_step(cuda):
             if use_host:
                 sm.step_from_host(host)
             else:
-                lay.slot_view(grads, 0).copy_(host)
+                lay.load_slot(grads, 0, host)
                 sm.step()
         torch.cuda.synchronize(cuda)
         out.append(params.cpu())

@@ -125,15 +125,16 @@ def test_lpt_assignment_balances_llama_matrices():
 
 def test_shard_layout_is_disjoint_and_grouped():
     shapes = [(64, 96), (96, 64), (64, 96), (32, 32), (64, 96), (16, 48)]
-    for world in (1, 2, 3):
-        lay = ShardLayout(shapes, world)
+    for world, chunks in ((1, None), (2, None), (3, 2), (2, 5)):
+        lay = ShardLayout(shapes, world, chunks=chunks)
         flat = torch.zeros(lay.numel)
         seen = torch.zeros(lay.numel, dtype=torch.int32)
         for i, (r, c) in enumerate(shapes):
             v = lay.matrix(flat, i)
             assert tuple(v.shape) == (r, c)
             rank, off = lay.offset_of[i]
-            assert rank * lay.slot <= off and off + r * c <= (rank + 1) * lay.slot
+            parts = [(lay.chunk_base[k] + rank * lay.chunk_len[k], lay.chunk_len[k]) for k in range(lay.chunks)]
+            assert any(s <= off and off + r * c <= s + n for s, n in parts)  # inside one of its rank's chunk parts
             seen[off:off + r * c] += 1
         assert int(seen.max()) == 1
         for rank in range(world):
@@ -162,7 +163,7 @@ def test_step_from_host_matches_copy_then_step_on_cpu():
         if use_host:
             sm.step_from_host(host)
         else:
-            lay.slot_view(grads, 0).copy_(host)
+            lay.load_slot(grads, 0, host)
             sm.step()
         out.append(params.clone())
     assert torch.equal(out[0], out[1])
