@@ -290,7 +290,8 @@ def run_ours(args, rank, world, local_rank):
             "config": {"workload": "Muon step over Llama-3-8B matrix params (224 bf16 matrices, 5 NS steps)",
                        "ns_steps": 5, "momentum": 0.95, "nesterov": True,
                        "parallelism": f"per-matrix FLOP-balanced shard x{world} + NCCL all-gather"
-                                      + (f" in {layout.chunks} chunks overlapped with the step" if world > 1 else ""),
+                                      + (f" in {layout.chunks} chunks overlapped with the step"
+                                         if world > 1 and layout.chunks > 1 else ""),
                        "l2": "inputs larger than L2 (13.96 GB of bf16 params and grads per step)",
                        "algorithmic_tflop_per_step": round(total_flops / 1e12, 1)},
             "tflops": round(total_flops / (step_ms * 1e-3) / 1e12, 1),
