@@ -45,8 +45,8 @@ MEASURED_PEAKS = os.path.join(HERE, "MEASURED_PEAKS.json")
 # the Newton-Schulz product launches) of the two captured workloads; the
 # commands and per-kernel figures are in profiles/launches_llama8b_muon_step.md
 # and profiles/tc_gemm_pair_ns4096.md.
-LLAMA_STEP_TRAFFIC = 1_160_370_000_000   # bytes per 1-GPU step (823.4 GB read + 337.0 GB write)
-NS4096_CALL_TRAFFIC = 14_080_000_000     # bytes per NS5 call on 4 x 4096^2 (9.50 GB read + 4.58 GB write)
+LLAMA_STEP_TRAFFIC = 1_120_000_000_000   # bytes per 1-GPU step (808.5 GB read + 311.5 GB write)
+NS4096_CALL_TRAFFIC = 13_660_000_000     # bytes per NS5 call on 4 x 4096^2 (9.65 GB read + 4.01 GB write)
 
 def llama_shapes():
     return LLAMA_LAYER * 32
