@@ -150,6 +150,14 @@ size_t po_precond_workspace_bytes(long long m, long long n, int dtype);
 int po_precond_apply(const void* L, long long l_ld, const void* G, long long g_ld, const void* R, long long r_ld,
                      void* out, long long out_ld, int dtype, long long m, long long n, void* workspace,
                      size_t workspace_bytes, void* stream);
+/* Same product, and *sq_sum (device fp64, set here) = ||out||_F^2 computed by
+ * the second product's epilogue from the fp32 values it stores: the
+ * denominator of Shampoo's grafting ratio target / (||P|| + 1e-30)
+ * (pytorch_opt/optim/shampoo.py:128-137) without re-reading P or a separate
+ * norm kernel. Same workspace as po_precond_apply. */
+int po_precond_apply_norm(const void* L, long long l_ld, const void* G, long long g_ld, const void* R,
+                          long long r_ld, void* out, long long out_ld, int dtype, long long m, long long n,
+                          double* sq_sum, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
  * Elementwise halves of the Muon step, flat over n elements of `dtype`

@@ -74,6 +74,10 @@ struct Epilogue {
   EpiOut out[kMaxEpiOut];
   float* red_absmax;  // per batch: max |D_ij - red_ident * [i==j]| (nullable), fp32 bits >= 0
   float red_ident;
+  // Per batch: += sum of D_ij^2 over the stored values (nullable; products
+  // without mirrored tiles only, and never together with red_absmax: the
+  // per-thread reduction register serves one of the two).
+  double* red_sumsq;
   // Diagonal split of a symmetric product U V whose operands were passed to
   // the tensor cores with zeroed diagonals: the epilogue adds the diagonal's
   // exact contribution alpha * (u_i V_ij + U_ij v_j - [i==j] u_i v_i) from
@@ -455,6 +459,10 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCo
 #pragma unroll
     for (int j = 0; j < EC; ++j)
       if (col0 + j < N) red_update(red, fabsf(v[j] - (j == jd ? E.red_ident : 0.0f)));
+  } else if (E.red_sumsq != nullptr) {
+#pragma unroll
+    for (int j = 0; j < EC; ++j)
+      if (col0 + j < N) red = fmaf(v[j], v[j], red);
   }
   if (mirror && same) {
     // The full product is symmetric: the mirrored element takes the same value.
@@ -733,6 +741,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
         for (int o = 16; o > 0; o >>= 1) red = fmaxf(red, __shfl_xor_sync(0xffffffffu, red, o));
         if (lane == 0 && red > 0.0f)
           atomicMax(reinterpret_cast<int*>(P.epi.red_absmax) + tc.b, __float_as_int(red));
+      } else if (P.epi.red_sumsq != nullptr) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) red += __shfl_xor_sync(0xffffffffu, red, o);
+        if (lane == 0) atomicAdd(P.epi.red_sumsq + tc.b, static_cast<double>(red));
       }
     }
   }

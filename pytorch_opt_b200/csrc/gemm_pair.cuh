@@ -327,6 +327,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
         for (int o = 16; o > 0; o >>= 1) red = fmaxf(red, __shfl_xor_sync(0xffffffffu, red, o));
         if (lane == 0 && red > 0.0f)
           atomicMax(reinterpret_cast<int*>(P.epi.red_absmax) + tc.b, __float_as_int(red));
+      } else if (P.epi.red_sumsq != nullptr) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) red += __shfl_xor_sync(0xffffffffu, red, o);
+        if (lane == 0) atomicAdd(P.epi.red_sumsq + tc.b, static_cast<double>(red));
       }
     }
   }

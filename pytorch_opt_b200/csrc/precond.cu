@@ -55,11 +55,31 @@ extern "C" size_t po_precond_workspace_bytes(long long m, long long n, int dtype
   return ar.used + 256;
 }
 
+extern "C" int po_precond_apply_norm(const void* L, long long l_ld, const void* G, long long g_ld, const void* R,
+                                     long long r_ld, void* out, long long out_ld, int dtype, long long m,
+                                     long long n, double* sq_sum, void* workspace, size_t workspace_bytes,
+                                     void* stream);
+
 extern "C" int po_precond_apply(const void* L, long long l_ld, const void* G, long long g_ld, const void* R,
                                 long long r_ld, void* out, long long out_ld, int dtype, long long m, long long n,
                                 void* workspace, size_t workspace_bytes, void* stream) {
+  return po_precond_apply_norm(L, l_ld, G, g_ld, R, r_ld, out, out_ld, dtype, m, n, nullptr, workspace,
+                               workspace_bytes, stream);
+}
+
+// As po_precond_apply; with sq_sum (device fp64) also ||out||_F^2 summed by
+// the second product's epilogue over the values it stores (grafting norm).
+extern "C" int po_precond_apply_norm(const void* L, long long l_ld, const void* G, long long g_ld, const void* R,
+                                     long long r_ld, void* out, long long out_ld, int dtype, long long m,
+                                     long long n, double* sq_sum, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
   if (dtype != PO_F32 && dtype != PO_BF16) return set_error(PO_ERR_ARG, "precond_apply: dtype must be fp32 or bf16");
   if (m < 0 || n < 0) return set_error(PO_ERR_ARG, "precond_apply: negative size");
+  if (sq_sum != nullptr) {
+    const int rz = check_cuda(cudaMemsetAsync(sq_sum, 0, sizeof(double), static_cast<cudaStream_t>(stream)),
+                              "memset");
+    if (rz) return rz;
+  }
   if (m == 0 || n == 0) return PO_OK;
   if (!L || !G || !R || !out) return set_error(PO_ERR_ARG, "precond_apply: null pointer");
   if (l_ld < m || g_ld < n || r_ld < n || out_ld < n) return set_error(PO_ERR_ARG, "precond_apply: pitch too small");
@@ -119,5 +139,6 @@ extern "C" int po_precond_apply(const void* L, long long l_ld, const void* G, lo
   g2.epi.alpha = 1.0f;
   g2.epi.nout = 1;
   g2.epi.out[0] = epi_out(out, dtype == PO_F32 ? OUT_F32 : OUT_BF16, out_ld, m * out_ld);
+  g2.epi.red_sumsq = sq_sum;  // sums the fp32 values before the store's rounding
   return launch_gemm(g2, s);
 }

@@ -149,6 +149,10 @@ def kron_factor_update_(L: torch.Tensor, R: torch.Tensor, G: torch.Tensor, beta2
 
 def precond_apply_two_sided(L_root: torch.Tensor, G: torch.Tensor, R_root: torch.Tensor) -> torch.Tensor:
     """L_root @ G @ R_root (reference.py:117-121, cpp:96-99)."""
+    return _precond(L_root, G, R_root, False)[0]
+
+
+def _precond(L_root, G, R_root, want_norm: bool):
     dev = _require_cuda(L_root, G, R_root)
     if G.dim() != 2 or L_root.dim() != 2 or R_root.dim() != 2:
         raise RuntimeError("precond_apply_two_sided expects 2D operands")
@@ -158,15 +162,35 @@ def precond_apply_two_sided(L_root: torch.Tensor, G: torch.Tensor, R_root: torch
     dt = G.dtype if G.dtype in (torch.float32, torch.bfloat16) else torch.float32
     Lc, Gc, Rc = (t.to(dt).contiguous() for t in (L_root, G, R_root))
     out = torch.empty(m, n, dtype=dt, device=dev)
+    sq = torch.zeros((), dtype=torch.float64, device=dev) if want_norm else None
     if m and n:
         with torch.cuda.device(dev):
             lib = _lib.load()
             code = _lib.DTYPE_CODE[dt]
             nbytes = lib.po_precond_workspace_bytes(m, n, code)
             ws = _lib.workspace(nbytes, dev)
-            _call("po_precond_apply", Lc.data_ptr(), m, Gc.data_ptr(), n, Rc.data_ptr(), n, out.data_ptr(), n, code,
-                  m, n, ws.data_ptr(), nbytes, _lib.stream_ptr(dev))
-    return out if out.dtype == G.dtype else out.to(G.dtype)
+            if want_norm:
+                _call("po_precond_apply_norm", Lc.data_ptr(), m, Gc.data_ptr(), n, Rc.data_ptr(), n, out.data_ptr(),
+                      n, code, m, n, sq.data_ptr(), ws.data_ptr(), nbytes, _lib.stream_ptr(dev))
+            else:
+                _call("po_precond_apply", Lc.data_ptr(), m, Gc.data_ptr(), n, Rc.data_ptr(), n, out.data_ptr(), n,
+                      code, m, n, ws.data_ptr(), nbytes, _lib.stream_ptr(dev))
+    return (out if out.dtype == G.dtype else out.to(G.dtype)), sq
+
+
+def precond_apply_grafted(L_root: torch.Tensor, G: torch.Tensor, R_root: torch.Tensor,
+                          target: torch.Tensor | float) -> tuple[torch.Tensor, torch.Tensor]:
+    """Shampoo's preconditioned direction with grafting (``optim/shampoo.py:126-137``).
+
+    Returns ``(P * ratio, ratio)`` with ``P = L_root @ G @ R_root`` and
+    ``ratio = target / (||P||_F + 1e-30)``; ``target`` is the grafted norm
+    (``||G||`` for "sgd", the AdaGrad direction's norm for "adagrad"). The
+    norm comes from the product's epilogue, and ``ratio`` stays a device
+    scalar (the reference reads it back with ``float()``).
+    """
+    P, sq = _precond(L_root, G, R_root, True)
+    ratio = (torch.as_tensor(target, dtype=torch.float64, device=P.device) / (sq.sqrt() + 1e-30))
+    return P.mul_(ratio.to(P.dtype)), ratio
 
 
 # --------------------------------------------------------------------------

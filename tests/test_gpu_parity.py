@@ -282,6 +282,23 @@ def test_precond_golden_and_oracle(cuda):
     assert _rel(_np(got), O.precond_apply(_np(L).astype(np.float64), _np(G), _np(R))) <= FACTOR_TOL
 
 
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_precond_grafted_norm_from_epilogue(cuda, dt):
+    """Grafting (shampoo.py:128-137): the epilogue's ||P||^2 matches the norm of
+    the returned product and P * ratio matches the plain apply scaled on the host."""
+    g = torch.Generator().manual_seed(4)
+    L, G, R = torch.randn(640, 640, generator=g), torch.randn(640, 1100, generator=g), torch.randn(1100, 1100, generator=g)
+    L, G, R = (t.to(cuda, dt) for t in (L, G, R))
+    plain = native.precond_apply_two_sided(L, G, R)
+    target = float(G.double().norm())
+    P, ratio = native.precond_apply_grafted(L, G, R, target)
+    # The epilogue sums the fp32 values before the output's rounding.
+    want_ratio = target / (float(plain.double().norm()) + 1e-30)
+    assert abs(float(ratio) - want_ratio) <= (1e-5 if dt == torch.float32 else 2e-3) * want_ratio
+    np.testing.assert_allclose(_np(P), _np(plain) * float(ratio), rtol=1e-2 if dt == torch.bfloat16 else 1e-6,
+                               atol=1e-30)
+
+
 # ------------------------------------------------------------------------ Muon
 
 def _bf16_ulps(got, want, ref_scale):
