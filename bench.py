@@ -539,6 +539,31 @@ def run_secondary(args, rank):
               fl_u / (ms_u * 1e-3) / 1e12, clk, None, cpu,
               {"ms_per_step": round(ms_u, 4), "damped_inverse_ms_both": round(ms_i, 3)})
         return 0
+    if w == "ekfac":       # section 8f rank 4: EKFAC rotated-diagonal precondition of one layer
+        m = n = 4096
+        g = torch.Generator(device=dev).manual_seed(6)
+        QG = torch.linalg.qr(torch.randn(m, m, generator=g, device=dev))[0]
+        QA = torch.linalg.qr(torch.randn(n, n, generator=g, device=dev))[0]
+        V = torch.randn(m, n, generator=g, device=dev)
+        _, S = native.ekfac_precondition(QG, QA, V, None, 0.95, 1e-3)
+        ms, clk = _timed(lambda: native.ekfac_precondition(QG, QA, V, S, 0.95, 1e-3), args.steps, args.warmup, dev,
+                         flush)
+        fl = 4 * 2.0 * m * n * 4096
+        cpu = None
+        if not args.no_cpu_baseline:
+            from oracle import ops_np as O
+            k = 1024  # bounded sample: the same four products at a quarter of each dimension
+            qg, qa, v = QG[:k, :k].cpu().numpy(), QA[:k, :k].cpu().numpy(), V[:k, :k].cpu().numpy()
+            _, s0 = O.ekfac_precondition(qg, qa, v, None, 0.95, 1e-3)
+            t = _cpu_time(lambda: O.ekfac_precondition(qg, qa, v, s0, 0.95, 1e-3))
+            cpu = {"value": round(t * 1e3 * 64, 1), "unit": "ms", "cores": threads, "kind": "port",
+                   "sample": "the numpy restatement of ekfac.py:44-58 (fp32 BLAS) on 1024x1024 blocks, x64 for the "
+                             "4096^2 layer by dense FLOPs"}
+        _line(args, "EKFAC precondition ms (one 4096x4096 layer)", ms, "ms", False,
+              "EKFAC QG (Vt / (s + 1e-3)) QA^T with Vt = QG^T V QA and the running scales updated in place, "
+              "fp32 4096x4096, split-bf16 products", fl / (ms * 1e-3) / 1e12, clk, (4 + 3) * args.steps, cpu,
+              {"ms_per_step": round(ms, 4)})
+        return 0
     raise SystemExit(f"unknown workload {w}")
 
 
@@ -551,7 +576,7 @@ def main(argv=None) -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="llama8b",
-                    choices=("llama8b", "ns768", "ns4096", "gpt2", "shampoo", "kfac", "gemm"),
+                    choices=("llama8b", "ns768", "ns4096", "gpt2", "shampoo", "kfac", "gemm", "ekfac"),
                     help="llama8b (default, config 5); the others are single-GPU measurements of configs 1-4, "
                          "the 4x4096^2 profiling case and the bare product kernel (gemm)")
     ap.add_argument("--gemm", type=int, nargs=3, default=(8192, 8192, 8192), metavar=("M", "N", "K"),

@@ -160,6 +160,20 @@ int po_precond_apply_norm(const void* L, long long l_ld, const void* G, long lon
                           double* sq_sum, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * EKFAC preconditioning of one layer's gradient V (m x n, fp32): replaces
+ * EKFAC._precondition, pytorch_opt/optim/ekfac.py:44-58:
+ *   Vt = QG^T V QA; S <- first ? Vt^2 : decay*S + (1-decay)*Vt^2 (in place);
+ *   out = QG (Vt / (S + lam)) QA^T.
+ * QG m x m, QA n x n (the factors' eigenbases), S and out m x n, all fp32
+ * row-major with the given pitches; products on split-bf16 operands.
+ * ---------------------------------------------------------------------- */
+size_t po_ekfac_workspace_bytes(long long m, long long n);
+int po_ekfac_precondition(const float* QG, long long qg_ld, const float* QA, long long qa_ld, const float* V,
+                          long long v_ld, float* S, long long s_ld, float* out, long long out_ld, long long m,
+                          long long n, int first, float decay, float lam, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/* ------------------------------------------------------------------------
  * Elementwise halves of the Muon step, flat over n elements of `dtype`
  * (PO_F32 / PO_BF16), rounding after each in-place op like the reference's
  * pytorch_opt/optim/muon.py:82-83 and :87-92.

@@ -209,6 +209,27 @@ def kfac_damped_inverse(F, gamma: float):
     return inv, cond
 
 
+def ekfac_precondition(QG, QA, V, scale, decay: float, damping: float):
+    """EKFAC's rotated-diagonal preconditioning (pytorch_opt/optim/ekfac.py:44-58).
+
+    Vt = QG^T V QA (:51, in the eigenbases' dtype); the running second
+    moments start as Vt^2 (:53-55) or take decay*s + (1-decay)*Vt^2 (:57);
+    returns (QG (Vt / (s + damping)) QA^T, s) (:58). ``scale`` None = first
+    call. Computed in the eigenbases' dtype (fp32 here) like the reference.
+    """
+    QG = np.asarray(QG)
+    work = QG.dtype
+    QA = np.asarray(QA, dtype=work)
+    V = np.asarray(V, dtype=work)
+    Vt = QG.T @ V @ QA
+    sq = Vt * Vt
+    if scale is None:
+        s = sq.copy()
+    else:
+        s = (np.asarray(scale, dtype=work) * work.type(decay) + work.type(1.0 - decay) * sq).astype(work)
+    return (QG @ (Vt / (s + work.type(damping))) @ QA.T).astype(work), s
+
+
 def muon_scale(shape, lr_adjust: str = "spectral") -> float:
     """Update scale (pytorch_opt/optim/muon.py:51-58)."""
     m, n = shape[-2], shape[-1]

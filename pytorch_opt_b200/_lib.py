@@ -40,6 +40,9 @@ SIGNATURES = {
     "po_precond_workspace_bytes": (_sz, [_ll, _ll, _i]),
     "po_precond_apply": (_i, [_vp, _ll, _vp, _ll, _vp, _ll, _vp, _ll, _i, _ll, _ll, _vp, _sz, _vp]),
     "po_precond_apply_norm": (_i, [_vp, _ll, _vp, _ll, _vp, _ll, _vp, _ll, _i, _ll, _ll, _vp, _vp, _sz, _vp]),
+    "po_ekfac_workspace_bytes": (_sz, [_ll, _ll]),
+    "po_ekfac_precondition": (_i, [_vp, _ll, _vp, _ll, _vp, _ll, _vp, _ll, _vp, _ll, _ll, _ll, _i, _f, _f, _vp, _sz,
+                                   _vp]),
     "po_muon_momentum": (_i, [_vp, _vp, _vp, _i, _ll, _f, _i, _vp]),
     "po_muon_apply": (_i, [_vp, _vp, _i, _ll, _f, _f, _vp, _vp]),
     "po_matmul_workspace_bytes": (_sz, [_ll, _ll, _ll, _ll, _i, _i]),

@@ -192,6 +192,7 @@ int launch_gemm(const GemmDesc& d, cudaStream_t stream) {
   if (d.M <= 0 || d.N <= 0 || d.batch <= 0) return PO_OK;
   if (d.K <= 0) return set_error(PO_ERR_ARG, "launch_gemm: K must be positive");
   if (d.tri && d.M != d.N) return set_error(PO_ERR_ARG, "launch_gemm: triangular product needs M == N");
+  if (d.epi.ek_s != nullptr && d.tri) return set_error(PO_ERR_ARG, "launch_gemm: the EKFAC epilogue needs a plain product");
   if (d.epi.red_sumsq != nullptr && (d.tri || d.epi.red_absmax != nullptr))
     return set_error(PO_ERR_ARG, "launch_gemm: the sum-of-squares reduction needs a plain product");
   if (d.npass != 1 && d.npass != 3) return set_error(PO_ERR_ARG, "launch_gemm: npass must be 1 or 3");

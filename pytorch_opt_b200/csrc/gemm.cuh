@@ -78,6 +78,13 @@ struct Epilogue {
   // without mirrored tiles only, and never together with red_absmax: the
   // per-thread reduction register serves one of the two).
   double* red_sumsq;
+  // EKFAC rescaling of the product Vt (pytorch_opt/optim/ekfac.py:51-58), on
+  // plain products only: in place S <- first ? Vt^2 : decay*S + (1-decay)*Vt^2
+  // (fp32, S shaped like the output), then the outputs receive Vt / (S + lam).
+  float* ek_s;
+  long long ek_ld, ek_bstride;
+  float ek_decay, ek_lam;
+  int ek_first;
   // Diagonal split of a symmetric product U V whose operands were passed to
   // the tensor cores with zeroed diagonals: the epilogue adds the diagonal's
   // exact contribution alpha * (u_i V_ij + U_ij v_j - [i==j] u_i v_i) from
@@ -452,6 +459,18 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCo
 #pragma unroll
   for (int i = 0; i < kMaxEpiIn; ++i)
     if (i < E.nin) add_row(E.in[i], tc.b, row, col0, N, v);
+  if (E.ek_s != nullptr) {
+    float* sp = E.ek_s + static_cast<long long>(tc.b) * E.ek_bstride + static_cast<long long>(row) * E.ek_ld + col0;
+#pragma unroll
+    for (int j = 0; j < EC; ++j) {
+      if (col0 + j < N) {
+        const float sq = v[j] * v[j];                                            // Vt.pow(2)
+        const float sn = E.ek_first ? sq : fmaf(1.0f - E.ek_decay, sq, sp[j] * E.ek_decay);  // s.mul_().add_()
+        sp[j] = sn;
+        v[j] = v[j] / (sn + E.ek_lam);                                           // Vt / (s + lam)
+      }
+    }
+  }
 #pragma unroll
   for (int o = 0; o < kMaxEpiOut; ++o)
     if (o < E.nout) store_out(E.out[o], tc.b, row, col0, N, jd, v);

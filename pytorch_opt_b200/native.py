@@ -258,3 +258,39 @@ def _eigh_root(A: torch.Tensor, p: int, damping: float, root_f64: bool) -> torch
     evals = evals.clamp_min(1e-30)
     root = evecs @ torch.diag_embed(evals.pow(-1.0 / p)) @ evecs.mT
     return (0.5 * (root + root.mT)).to(orig)
+
+
+def ekfac_precondition(QG: torch.Tensor, QA: torch.Tensor, V: torch.Tensor, scale: torch.Tensor | None,
+                       decay: float, damping: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """EKFAC's rotated-diagonal preconditioning (``optim/ekfac.py:44-58``).
+
+    ``QG`` (m x m) and ``QA`` (n x n) are the factors' eigenbases, ``V`` the
+    m x n gradient, ``scale`` the running second moments of the rotated
+    gradient (``None`` on the first call: they start as ``Vt**2``; otherwise
+    updated in place with ``decay``). Returns ``(QG (Vt / (scale + damping))
+    QA^T, scale)`` in ``V``'s dtype; the work runs in fp32 like the reference
+    (which casts ``V`` to the eigenbases' dtype).
+    """
+    dev = _require_cuda(QG, QA, V)
+    if V.dim() != 2 or QG.dim() != 2 or QA.dim() != 2:
+        raise RuntimeError("ekfac_precondition expects 2D operands")
+    m, n = V.shape
+    if tuple(QG.shape) != (m, m) or tuple(QA.shape) != (n, n):
+        raise RuntimeError("ekfac_precondition: shape mismatch")
+    QGc, QAc, Vc = (t.to(torch.float32).contiguous() for t in (QG, QA, V))
+    first = scale is None
+    if first:
+        scale = torch.empty(m, n, dtype=torch.float32, device=dev)
+    elif scale.dtype != torch.float32 or tuple(scale.shape) != (m, n) or not scale.is_contiguous():
+        raise RuntimeError("ekfac_precondition: scale must be a contiguous fp32 (m, n) tensor")
+    out = torch.empty(m, n, dtype=torch.float32, device=dev)
+    if m and n:
+        with torch.cuda.device(dev):
+            lib = _lib.load()
+            nbytes = lib.po_ekfac_workspace_bytes(m, n)
+            ws = _lib.workspace(nbytes, dev)
+            _call("po_ekfac_precondition", QGc.data_ptr(), m, QAc.data_ptr(), n, Vc.data_ptr(), n, scale.data_ptr(), n,
+                  out.data_ptr(), n, m, n, 1 if first else 0, float(decay), float(damping), ws.data_ptr(), nbytes,
+                  _lib.stream_ptr(dev))
+    return (out if V.dtype == torch.float32 else out.to(V.dtype)), scale
+

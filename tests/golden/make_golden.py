@@ -184,17 +184,55 @@ def make_muon(Muon) -> dict:
     return out
 
 
-def main() -> None:
+def make_ekfac() -> dict:
+    """EKFAC._precondition (optim/ekfac.py:44-58) on two consecutive gradients.
+
+    The method is called unbound on a stand-in holding exactly the state it
+    reads (eigenbases, damping, running scales, decay), so no model or hooks
+    are needed; eigenbases come from fp64 eigh of SPD factors, as in
+    ``_refresh_inverses`` (:27-42).
+    """
+    from types import SimpleNamespace
+    from pytorch_opt.optim.ekfac import EKFAC
+    out = {}
+    cases = [(48, 80, 0.95, 1e-3), (96, 33, 0.9, 1e-2)]
+    for i, (m, n, decay, lam) in enumerate(cases):
+        _, QG = torch.linalg.eigh(_spd(m, 300 + i))
+        _, QA = torch.linalg.eigh(_spd(n, 400 + i))
+        QG, QA = QG.to(torch.float32), QA.to(torch.float32)
+        me = SimpleNamespace(_inv={"w": {"QG": QG, "QA": QA}}, param_groups=[{"damping": lam}], _scales={},
+                             _scale_decay=decay)
+        g = torch.Generator().manual_seed(500 + i)
+        V1 = torch.randn(m, n, generator=g)
+        V2 = torch.randn(m, n, generator=g)
+        o1 = EKFAC._precondition(me, "w", V1)
+        s1 = me._scales["w"].clone()
+        o2 = EKFAC._precondition(me, "w", V2)
+        s2 = me._scales["w"].clone()
+        out.update({f"case{i}_QG": _f32(QG), f"case{i}_QA": _f32(QA), f"case{i}_V1": _f32(V1),
+                    f"case{i}_V2": _f32(V2), f"case{i}_out1": _f32(o1), f"case{i}_out2": _f32(o2),
+                    f"case{i}_s1": _f32(s1), f"case{i}_s2": _f32(s2),
+                    f"case{i}_hp": np.array([decay, lam], dtype=np.float64)})
+    out["ncases"] = np.array(len(cases))
+    return out
+
+
+def main(only=None) -> None:
+    """Write every fixture, or only the named ones (e.g. ``ekfac``)."""
     R, KronTracker, kfac_factored_damping, KFAC, Muon = _import_reference()
     torch.set_num_threads(1)
-    np.savez_compressed(os.path.join(HERE, "ns.npz"), **make_ns(R))
-    np.savez_compressed(os.path.join(HERE, "roots.npz"), **make_roots(R))
-    np.savez_compressed(os.path.join(HERE, "kron.npz"), **make_kron(R))
-    np.savez_compressed(os.path.join(HERE, "precond.npz"), **make_precond(R))
-    np.savez_compressed(os.path.join(HERE, "kfac.npz"), **make_kfac(KronTracker, kfac_factored_damping, KFAC))
-    np.savez_compressed(os.path.join(HERE, "muon.npz"), **make_muon(Muon))
+    makers = {
+        "ns": lambda: make_ns(R), "roots": lambda: make_roots(R), "kron": lambda: make_kron(R),
+        "precond": lambda: make_precond(R),
+        "kfac": lambda: make_kfac(KronTracker, kfac_factored_damping, KFAC), "muon": lambda: make_muon(Muon),
+        "ekfac": make_ekfac,
+    }
+    for name, make in makers.items():
+        if only and name not in only:
+            continue
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **make())
     print("golden fixtures written to", HERE)
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:] or None)

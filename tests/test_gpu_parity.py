@@ -299,6 +299,38 @@ def test_precond_grafted_norm_from_epilogue(cuda, dt):
                                atol=1e-30)
 
 
+EKFAC_SCALE_TOL = 1e-4  # the running second moments: a factor-update-like statistic
+# The output divides Vt by (s + damping): where Vt ~ sqrt(damping) the
+# rounding of the split-bf16 products (~4e-6 relative in Vt) is amplified
+# by up to ~1/(2 sqrt(damping)); measured 3e-5 .. 1.5e-4 against the
+# reference's fp32 result and 6e-5 against fp64.
+EKFAC_OUT_TOL = 5e-4
+
+
+def test_ekfac_precondition_golden_and_oracle(cuda):
+    """EKFAC (ekfac.py:44-58) on two consecutive gradients: the first call
+    seeds the running scales, the second updates them in place."""
+    z = np.load(os.path.join(GOLDEN_DIR, "ekfac.npz"))
+    for i in range(int(z["ncases"])):
+        decay, lam = (float(v) for v in z[f"case{i}_hp"])
+        QG, QA = (torch.from_numpy(z[f"case{i}_{k}"]).to(cuda) for k in ("QG", "QA"))
+        o1, s = native.ekfac_precondition(QG, QA, torch.from_numpy(z[f"case{i}_V1"]).to(cuda), None, decay, lam)
+        assert _rel(_np(o1), z[f"case{i}_out1"]) <= EKFAC_OUT_TOL and _rel(_np(s), z[f"case{i}_s1"]) <= EKFAC_SCALE_TOL
+        o2, s = native.ekfac_precondition(QG, QA, torch.from_numpy(z[f"case{i}_V2"]).to(cuda), s, decay, lam)
+        assert _rel(_np(o2), z[f"case{i}_out2"]) <= EKFAC_OUT_TOL and _rel(_np(s), z[f"case{i}_s2"]) <= EKFAC_SCALE_TOL
+    # A layer-sized case (ragged tiles, long K) against the oracle in fp64.
+    g = torch.Generator().manual_seed(8)
+    m, n = 700, 1300
+    QG = torch.linalg.qr(torch.randn(m, m, generator=g, dtype=torch.float64))[0].float()
+    QA = torch.linalg.qr(torch.randn(n, n, generator=g, dtype=torch.float64))[0].float()
+    V1, V2 = torch.randn(m, n, generator=g), torch.randn(m, n, generator=g)
+    o1, s = native.ekfac_precondition(QG.to(cuda), QA.to(cuda), V1.to(cuda), None, 0.95, 1e-3)
+    o2, s = native.ekfac_precondition(QG.to(cuda), QA.to(cuda), V2.to(cuda), s, 0.95, 1e-3)
+    w1, ws = O.ekfac_precondition(_np(QG).astype(np.float64), _np(QA), _np(V1), None, 0.95, 1e-3)
+    w2, ws = O.ekfac_precondition(_np(QG).astype(np.float64), _np(QA), _np(V2), ws, 0.95, 1e-3)
+    assert _rel(_np(o2), w2) <= EKFAC_OUT_TOL and _rel(_np(s), ws) <= EKFAC_SCALE_TOL
+
+
 # ------------------------------------------------------------------------ Muon
 
 def _bf16_ulps(got, want, ref_scale):

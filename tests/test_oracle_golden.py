@@ -119,3 +119,16 @@ def test_bf16_round_matches_torch():
     x[:4] = [0.0, -0.0, 1e-40, 3.0e38]
     want = torch.from_numpy(x).bfloat16().float().numpy()
     np.testing.assert_array_equal(O.bf16_round(x), want)
+
+
+def test_ekfac_oracle_matches_reference_golden():
+    z = np.load(os.path.join(GOLDEN_DIR, "ekfac.npz"))
+    for i in range(int(z["ncases"])):
+        decay, lam = (float(v) for v in z[f"case{i}_hp"])
+        QG, QA = z[f"case{i}_QG"], z[f"case{i}_QA"]
+        o1, s1 = O.ekfac_precondition(QG, QA, z[f"case{i}_V1"], None, decay, lam)
+        o2, s2 = O.ekfac_precondition(QG, QA, z[f"case{i}_V2"], s1, decay, lam)
+        for got, key in ((o1, "out1"), (s1, "s1"), (o2, "out2"), (s2, "s2")):
+            want = z[f"case{i}_{key}"]
+            assert np.linalg.norm(got - want) / np.linalg.norm(want) <= 1e-5, (i, key)
+
