@@ -11,7 +11,8 @@
 // * Eight epilogue warps drain TMEM with tcgen05.ld and apply a fused
 //   "alpha*acc + sum(beta_i*C_i) + gamma*I" with up to three typed outputs,
 //   optional mirrored stores (symmetric products computed on the lower
-//   triangle of tiles only) and an optional per-batch max|D - ident*I|.
+//   triangle of tiles only), an optional per-batch max|D - ident*I| or
+//   sum of D^2, the exact diagonal split, and the EKFAC rescaling.
 // * Split-bf16 ("bf16x3") products: npass = 3 runs the K loop three times,
 //   hi*hi + hi*lo + lo*hi, into the same accumulator.
 //
