@@ -190,8 +190,9 @@ int po_muon_apply(void* p, const void* o, int dtype, long long n, float lr_eff, 
  * General batched product used by the ops above, exported for tests:
  *   C[b] = alpha * op(A[b]) @ op(B[b]) + beta * C[b]
  * A: M x K (trans_a: stored K x M), B: K x N (trans_b: stored N x K), all of
- * `dtype` PO_BF16 (bf16 products) or PO_F32 (precision: 0 = tf32,
- * 1 = split-bf16). C is fp32. Pitches in elements.
+ * `dtype` PO_BF16 (bf16 products; precision 1 = sum K in chunks outside the
+ * truncating tensor-core accumulator, for long K) or PO_F32 (precision:
+ * 0 = tf32, 1 = split-bf16, chunked). C is fp32. Pitches in elements.
  * ---------------------------------------------------------------------- */
 size_t po_matmul_workspace_bytes(long long batch, long long M, long long N, long long K, int dtype, int precision);
 int po_matmul(const void* A, long long lda, long long sa, int trans_a, const void* B, long long ldb, long long sb,

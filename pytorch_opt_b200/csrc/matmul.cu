@@ -110,7 +110,9 @@ extern "C" int po_matmul(const void* A, long long lda, long long sa, int trans_a
   g.b_kmajor = trans_b;   // B stored [N][K] is K-major
   g.kind = (dtype == PO_BF16 || split) ? KIND_BF16 : KIND_TF32;
   g.npass = split ? 3 : 1;
-  g.chunked = split;  // the precise mode also sums K chunks outside the truncating accumulator
+  // The precise mode also sums K chunks outside the truncating accumulator
+  // (for bf16 operands, precision 1 asks for that chunked accumulation alone).
+  g.chunked = precision == 1;
   g.sched = sched;
   int r;
   if ((r = zero_sched(sched, s))) return r;

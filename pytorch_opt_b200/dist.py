@@ -326,3 +326,95 @@ class ShardedMuon:
             eff = self.hp["lr"] * muon_scale(*grp.shape, self.hp["lr_adjust"])
             total += sq[k] * eff * eff
         return total
+
+
+# --------------------------------------------------------------------------
+# KFAC factor statistics split across GPUs by row bands of the output.
+# --------------------------------------------------------------------------
+
+def kfac_band_bounds(d: int, world: int, align: int = 16) -> list[int]:
+    """Row boundaries 0 = r_0 <= ... <= r_world = d of the bands of a d x d factor.
+
+    Band k is the rectangle rows [r_k, r_k+1) x columns [0, r_k+1): its rows of
+    the lower triangle plus the upper part of its own diagonal block. The
+    boundaries give every band about the same area (r_k+1 - r_k) * r_k+1, the
+    work of its product; they are multiples of ``align`` (16 keeps bf16 and
+    fp32 column offsets 16-byte aligned).
+    """
+    if world < 1:
+        raise ValueError("world must be >= 1")
+
+    def cut(target: float) -> list[int]:
+        out = [0]
+        while out[-1] < d and len(out) <= world:
+            r0 = out[-1]
+            r = r0 + align
+            while r < d and (r - r0) * r < target:
+                r += align
+            out.append(min(r, d))
+        return out
+
+    lo, hi = 0.0, float(d) * d
+    for _ in range(60):  # smallest band area with which world bands reach d
+        mid = 0.5 * (lo + hi)
+        if cut(mid)[-1] >= d and len(cut(mid)) <= world + 1:
+            hi = mid
+        else:
+            lo = mid
+    out = cut(hi)
+    while len(out) < world + 1:
+        out.append(d)
+    return out
+
+
+def _band_product(band: torch.Tensor, X: torch.Tensor, r0: int, r1: int, alpha: float, beta: float) -> None:
+    """band (rows r0..r1 of F, columns 0..r1) <- alpha X[:, r0:r1]^T X[:, :r1] + beta band, on the tensor cores."""
+    from . import _lib
+    lib = _lib.load()
+    rows, d = X.shape
+    code = _lib.DTYPE_CODE[X.dtype]
+    M, N = r1 - r0, r1
+    nbytes = lib.po_matmul_workspace_bytes(1, M, N, rows, code, 1)
+    ws = _lib.workspace(nbytes, X.device)
+    # A = X[:, r0:r1] stored [K = rows][M] (trans_a), B = X[:, :r1] stored [K][N]; precision 1:
+    # split-bf16 for fp32 X, chunked fp32 accumulation for bf16 X (K = rows is long).
+    _lib.check(lib.po_matmul(X.data_ptr() + r0 * X.element_size(), d, rows * d, 1, X.data_ptr(), d, rows * d, 0,
+                             band.data_ptr(), band.stride(0), M * band.stride(0), code, 1, 1, M, N, rows,
+                             float(alpha), float(beta), ws.data_ptr(), nbytes, _lib.stream_ptr(X.device)),
+               "po_matmul")
+
+
+def sharded_syrk_ema_(F: torch.Tensor, X: torch.Tensor, alpha: float, beta: float, first: bool, rank: int = 0,
+                      world: int = 1, group=None, compute=None) -> torch.Tensor:
+    """KFAC factor update ``F <- first ? alpha X^T X : beta F + (1 - beta) alpha X^T X`` split across ranks.
+
+    The statistic of ``pytorch_opt/curvature/kron.py:95-113`` for one layer,
+    with its d x d output cut into row bands of equal work
+    (``kfac_band_bounds``): every rank holds the same ``F`` (fp32) and ``X``
+    (rows x d, fp32 or bf16), computes only its band on the tensor cores,
+    one ``all_reduce`` assembles the lower triangle, and each rank mirrors it
+    into the full symmetric ``F``. With ``world == 1`` it is one product over
+    the whole matrix. ``compute(band, X, r0, r1, alpha, beta)`` replaces the
+    tensor-core product (host-side tests over gloo).
+    """
+    if X.dim() != 2 or F.dim() != 2 or F.shape[0] != F.shape[1] or F.shape[0] != X.shape[1]:
+        raise RuntimeError("sharded_syrk_ema_: expects X (rows, d) and F (d, d)")
+    if F.dtype != torch.float32 or not F.is_contiguous():
+        raise RuntimeError("sharded_syrk_ema_: F must be a contiguous fp32 tensor")
+    d = F.shape[0]
+    bounds = kfac_band_bounds(d, world)
+    r0, r1 = bounds[rank], bounds[rank + 1]
+    Xw = (X if X.dtype in (torch.float32, torch.bfloat16) else X.float()).contiguous()
+    D = torch.zeros_like(F)
+    if r1 > r0:
+        band = D[r0:r1, :r1]
+        if not first:
+            band.copy_(F[r0:r1, :r1])
+        a_eff = alpha if first else (1.0 - beta) * alpha
+        b_eff = 0.0 if first else beta
+        (compute or _band_product)(band, Xw, r0, r1, a_eff, b_eff)
+    if world > 1:
+        dist.all_reduce(D, group=group)
+    F.copy_(torch.tril(D) + torch.tril(D, -1).mT)
+    return F
+

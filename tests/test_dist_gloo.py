@@ -61,6 +61,30 @@ def _worker_exchange(rank, world, port, q):
         q.put((rank, False, traceback.format_exc(), -1))
 
 
+def _worker_band_syrk(rank, world, port, q):
+    try:
+        from pytorch_opt_b200.dist import sharded_syrk_ema_
+        _init(rank, world, port)
+        g = torch.Generator().manual_seed(5)
+        X = torch.randn(64, 300, generator=g, dtype=torch.float64)
+        F = torch.zeros(300, 300, dtype=torch.float64)
+
+        def band_matmul(band, X, r0, r1, a, b):  # stands in for the tensor-core band product
+            band.mul_(b).add_(a * (X[:, r0:r1].T @ X[:, :r1]))
+
+        F32 = F.float()
+        sharded_syrk_ema_(F32, X.float(), 0.5, 0.9, True, rank, world, compute=band_matmul)
+        ok1 = torch.allclose(F32.double(), 0.5 * X.T @ X, rtol=1e-5, atol=1e-5)
+        X2 = torch.randn(64, 300, generator=g, dtype=torch.float64)
+        want = 0.9 * F32.double() + 0.1 * 0.5 * X2.T @ X2
+        sharded_syrk_ema_(F32, X2.float(), 0.5, 0.9, False, rank, world, compute=band_matmul)
+        ok2 = torch.allclose(F32.double(), want, rtol=1e-5, atol=1e-5) and torch.equal(F32, F32.T)
+        q.put((rank, bool(ok1 and ok2)))
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, traceback.format_exc()))
+
+
 def _worker_dead_peer(rank, world, port, q):
     try:
         _init(rank, world, port, timeout_s=5)
@@ -106,3 +130,9 @@ def test_dead_peer_surfaces_as_host_error():
     res = _run(_worker_dead_peer, 2)
     assert res[1][1] == "left"
     assert res[0][1].startswith("error:"), res[0][1]
+
+
+def test_band_split_factor_update_two_ranks():
+    res = _run(_worker_band_syrk, 2)
+    assert res[0][1] is True and res[1][1] is True, res
+

@@ -236,6 +236,27 @@ def test_kfac_syrk_ema_vs_oracle(cuda, rows, d, dt):
     assert _rel(_np(F), want) <= FACTOR_TOL
 
 
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_band_split_factor_update_one_rank(cuda, dt):
+    """The band-split factor update (one rank: one band product + mirror)
+    against the fused SYRK-EMA kernel and the oracle (first call and EMA)."""
+    from pytorch_opt_b200.dist import sharded_syrk_ema_
+    g = torch.Generator().manual_seed(21)
+    rows, d = 2048, 700
+    X1 = torch.randn(rows, d, generator=g).to(dt)
+    X2 = torch.randn(rows, d, generator=g).to(dt)
+    Fa = torch.empty(d, d, device=cuda)
+    Fb = torch.empty(d, d, device=cuda)
+    for X, first in ((X1, True), (X2, False)):
+        sharded_syrk_ema_(Fa, X.to(cuda), 1.0 / rows, 0.95, first)
+        native.kron_syrk_ema_(Fb, X.to(cuda), 1.0 / rows, 0.95, first)
+    assert _rel(_np(Fa), _np(Fb).astype(np.float64)) <= 1e-5
+    x1, x2 = _np(X1).astype(np.float64), _np(X2).astype(np.float64)
+    want = 0.95 * (x1.T @ x1 / rows) + 0.05 * (x2.T @ x2 / rows)
+    assert _rel(_np(Fa), want) <= FACTOR_TOL
+    assert torch.equal(Fa, Fa.T)
+
+
 def test_kfac_golden_factors_and_inverse(cuda):
     """Golden KronTracker factors (ghat = n g) and the damped inverse by the Newton kernel."""
     z = np.load(os.path.join(GOLDEN_DIR, "kfac.npz"))

@@ -170,3 +170,18 @@ def test_step_from_host_matches_copy_then_step_on_cpu():
     with pytest.raises(ValueError):
         ShardedMuon(lay, torch.zeros(lay.numel), torch.zeros(lay.numel), 0, compute=fake_update).step_from_host(
             host[:-1])
+
+
+def test_kfac_band_bounds_balance_the_triangle():
+    from pytorch_opt_b200.dist import kfac_band_bounds
+    for d in (4096, 1000, 300):
+        for world in (1, 2, 3, 4, 8):
+            b = kfac_band_bounds(d, world)
+            assert b[0] == 0 and b[-1] == d and len(b) == world + 1
+            assert all(x <= y for x, y in zip(b, b[1:]))
+            assert all(x % 16 == 0 or x == d for x in b[1:-1])
+            work = [(y - x) * y for x, y in zip(b, b[1:])]  # band rectangle areas
+            if d == 4096:
+                assert max(work) <= 1.05 * sum(work) / world
+                assert sum(work) <= d * d  # never more than the full square
+
