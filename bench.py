@@ -567,6 +567,69 @@ def run_secondary(args, rank):
     raise SystemExit(f"unknown workload {w}")
 
 
+def run_kfac_split(args, rank, world, local_rank):
+    """KFAC A and G factor updates (config 4 shapes) shared by all ranks: row bands + all_reduce."""
+    import torch.distributed as dist
+    from pytorch_opt_b200.dist import sharded_syrk_ema_
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    g1 = torch.Generator(device=dev).manual_seed(1)
+    g2 = torch.Generator(device=dev).manual_seed(2)
+    a = torch.randn(8192, 4096, generator=g1, device=dev).bfloat16()
+    gr = torch.randn(8192, 4096, generator=g2, device=dev).bfloat16()
+    A = torch.empty(4096, 4096, device=dev)
+    Gf = torch.empty(4096, 4096, device=dev)
+    n = 8192
+
+    def update(first=False):
+        sharded_syrk_ema_(A, a, 1.0 / n, 0.95, first, rank, world)
+        sharded_syrk_ema_(Gf, gr, float(n), 0.95, first, rank, world)
+    update(True)
+    for _ in range(args.warmup):
+        update()
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+    barrier()
+    clocks = ClockSampler(dev)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        update()
+    e1.record()
+    barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if rank == 0:
+        fl = 2 * 2.0 * 8192 * 4096 ** 2
+        pk = peaks()
+        tf = fl / (ms * 1e-3) / 1e12
+        print(json.dumps({
+            "metric": "KFAC factor update ms (A and G, 8192x4096 -> 4096^2), split by row bands", "value": round(ms, 4),
+            "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "KFAC SYRK+EMA of A and G shared by all ranks: row bands of equal work, "
+                                   "one all_reduce and a mirror per factor", "parallelism": f"row bands x{world}"},
+            "roofline": {"bound": "tensor", "kernel": "tc_gemm_kernel (chunked)", "achieved": round(tf, 1),
+                         "peak": pk["bf16_sustained"], "unit": "TFLOP/s", "frac": round(tf / pk["bf16_sustained"], 3),
+                         "traffic": None, "how": "dense SYRK FLOPs of both factors / the slowest rank's time"},
+            "clocks": clk, "gpu_launches": 2 * 2 * args.steps, "e2e": None, "cpu_baseline": None}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -576,7 +639,7 @@ def main(argv=None) -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="llama8b",
-                    choices=("llama8b", "ns768", "ns4096", "gpt2", "shampoo", "kfac", "gemm", "ekfac"),
+                    choices=("llama8b", "ns768", "ns4096", "gpt2", "shampoo", "kfac", "gemm", "ekfac", "kfac_split"),
                     help="llama8b (default, config 5); the others are single-GPU measurements of configs 1-4, "
                          "the 4x4096^2 profiling case and the bare product kernel (gemm)")
     ap.add_argument("--gemm", type=int, nargs=3, default=(8192, 8192, 8192), metavar=("M", "N", "K"),
@@ -590,6 +653,8 @@ def main(argv=None) -> int:
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference_arm(args, rank, world)
+    if args.workload == "kfac_split":
+        return run_kfac_split(args, rank, world, local_rank)
     if args.workload != "llama8b":
         return run_secondary(args, rank)
     return run_ours(args, rank, world, local_rank)
