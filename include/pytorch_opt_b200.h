@@ -57,12 +57,14 @@ const char* po_version(void);
  * divide by (||X||_F + eps), `steps` quintic iterations
  * A = X X^T, B = b A + c A^2, X = a X + B X, transpose back, cast to the
  * input dtype. G and out: [batch][rows][cols] of `dtype`
- * (PO_F32 / PO_BF16 / PO_F16 / PO_F64). The first (steps - tf32_tail)
- * iterations run bf16 tensor-core products, the last `tf32_tail` run tf32
- * products, all accumulating in fp32. tf32_tail < 0 selects the default
- * schedule by m = min(rows, cols): m >= 512: two tf32 steps after bf16 ones;
- * 256 <= m < 512: tf32 on every step; m < 256: split-bf16 pairs
- * (hi*hi + hi*lo + lo*hi) on every step.
+ * (PO_F32 / PO_BF16 / PO_F16 / PO_F64). Products accumulate in fp32.
+ * tf32_tail < 0 selects the default schedule by m = min(rows, cols):
+ * m >= 256: bf16 tensor-core products on every step, with the dominant
+ * diagonals of A and B kept out of the bf16 operands and added exactly in
+ * fp32 by the epilogues ("diagonal split"); m < 256: split-bf16 pairs
+ * (hi*hi + hi*lo + lo*hi) on every step. tf32_tail >= 0 runs the last
+ * `tf32_tail` steps on tf32 products and the others on bf16 (both with the
+ * diagonal split).
  * ---------------------------------------------------------------------- */
 size_t po_ns_workspace_bytes(long long batch, long long rows, long long cols);
 int po_newton_schulz(const void* G, int dtype, long long batch, long long rows, long long cols, long long ld,
@@ -103,7 +105,12 @@ int po_newton_schulz_static(const void* G, int dtype, long long batch, long long
  * split-bf16 (hi*hi + hi*lo + lo*hi, fp32 accumulate) while max|Mk - I| >
  * 1e-3 and as single bf16 afterwards; the iteration is carried in the
  * increment form E = Mk - I so that the stopping test sees the same values
- * as the fp64 reference. No host synchronisation happens inside.
+ * as the fp64 reference. Convergence is tracked on the device; iterations are
+ * enqueued in blocks of 4, after each of which the host reads one 4-byte
+ * count of items still iterating from the workspace (a stream
+ * synchronisation) and stops once it is zero. Under stream capture nothing
+ * is read back and all max_iter iterations are enqueued (converged items are
+ * skipped inside each launch).
  * A and out: [batch][d][d] of `dtype` (PO_F32 / PO_BF16 / PO_F64).
  * iters_out (nullable): device int[batch], iterations each item ran.
  * ---------------------------------------------------------------------- */
@@ -120,7 +127,8 @@ int po_inverse_root(const void* A, int dtype, long long batch, long long d, long
  * (beta2 == 1: plain sums). G: m x n (row pitch g_ld) of g_dtype
  * (PO_F32 / PO_BF16); L (m x m, pitch l_ld) and R (n x n, pitch r_ld) are
  * fp32. Only the lower triangle of tiles is computed; the upper triangle is
- * written by mirroring. fp32 G uses split-bf16 products.
+ * written by mirroring. fp32 G uses split-tf32 products (hi*hi + hi*lo +
+ * lo*hi on tf32 pairs, ~2^-21 relative: fp32-grade).
  * ---------------------------------------------------------------------- */
 size_t po_kron_workspace_bytes(long long m, long long n, int g_dtype);
 int po_kron_factor_update(float* L, long long l_ld, float* R, long long r_ld, const void* G, int g_dtype,
@@ -130,21 +138,26 @@ int po_kron_factor_update(float* L, long long l_ld, float* R, long long r_ld, co
 /* ------------------------------------------------------------------------
  * KFAC factor statistics with the exponential moving average fused:
  *   F <- first ? S : beta F + (1 - beta) S,   S = alpha * X^T X
- * X: rows x d (pitch x_ld) of x_dtype (PO_F32 / PO_BF16); F: d x d fp32.
+ * X: rows x d (pitch x_ld) of x_dtype (PO_F32 / PO_BF16; fp32 X runs as
+ * split-tf32 products, fp32-grade); F: d x d fp32.
  * Replaces pytorch_opt/curvature/kron.py:105-113 (_batch_factors, Linear:
  * A = a^T a / n with alpha = 1/n; G = ghat^T ghat / n with ghat = n g, i.e.
  * alpha = n) together with the EMA of kron.py:95-103 (first call clones).
+ * trace (device fp64, nullable) receives tr(F) of the updated factor, summed
+ * by the product's epilogue: the input of the pi-split damping of
+ * pytorch_opt/curvature/damping.py:10-25 without a pass over F.
  * ---------------------------------------------------------------------- */
 size_t po_syrk_workspace_bytes(long long rows, long long d, int x_dtype);
 int po_syrk_ema(float* F, long long d, long long f_ld, const void* X, int x_dtype, long long rows, long long x_ld,
-                double alpha, double beta, int first, void* workspace, size_t workspace_bytes, void* stream);
+                double alpha, double beta, int first, double* trace, void* workspace, size_t workspace_bytes,
+                void* stream);
 
 /* ------------------------------------------------------------------------
  * Two-sided preconditioner application out = L @ G @ R. Replaces
  * pytorch_opt/ops/csrc/pytorch_opt_ops.cpp:96-99 (bound at :110) and mirrors
  * pytorch_opt/ops/reference.py:117-121. All operands fp32 (or all bf16):
  * L m x m, G m x n, R n x n, out m x n, dense row-major with the given
- * pitches. fp32 operands use split-bf16 products.
+ * pitches. fp32 operands use split-tf32 products (fp32-grade).
  * ---------------------------------------------------------------------- */
 size_t po_precond_workspace_bytes(long long m, long long n, int dtype);
 int po_precond_apply(const void* L, long long l_ld, const void* G, long long g_ld, const void* R, long long r_ld,
@@ -165,7 +178,7 @@ int po_precond_apply_norm(const void* L, long long l_ld, const void* G, long lon
  *   Vt = QG^T V QA; S <- first ? Vt^2 : decay*S + (1-decay)*Vt^2 (in place);
  *   out = QG (Vt / (S + lam)) QA^T.
  * QG m x m, QA n x n (the factors' eigenbases), S and out m x n, all fp32
- * row-major with the given pitches; products on split-bf16 operands.
+ * row-major with the given pitches; products on split-tf32 operands.
  * ---------------------------------------------------------------------- */
 size_t po_ekfac_workspace_bytes(long long m, long long n);
 int po_ekfac_precondition(const float* QG, long long qg_ld, const float* QA, long long qa_ld, const float* V,
@@ -192,7 +205,8 @@ int po_muon_apply(void* p, const void* o, int dtype, long long n, float lr_eff, 
  * A: M x K (trans_a: stored K x M), B: K x N (trans_b: stored N x K), all of
  * `dtype` PO_BF16 (bf16 products; precision 1 = sum K in chunks outside the
  * truncating tensor-core accumulator, for long K) or PO_F32 (precision:
- * 0 = tf32, 1 = split-bf16, chunked). C is fp32. Pitches in elements.
+ * 0 = tf32, 1 = split-bf16 (~2^-16 relative), 2 = split-tf32 (~2^-21,
+ * fp32-grade); 1 and 2 chunked). C is fp32. Pitches in elements.
  * ---------------------------------------------------------------------- */
 size_t po_matmul_workspace_bytes(long long batch, long long M, long long N, long long K, int dtype, int precision);
 int po_matmul(const void* A, long long lda, long long sa, int trans_a, const void* B, long long ldb, long long sb,

@@ -36,7 +36,7 @@ SIGNATURES = {
     "po_kron_workspace_bytes": (_sz, [_ll, _ll, _i]),
     "po_kron_factor_update": (_i, [_vp, _ll, _vp, _ll, _vp, _i, _ll, _ll, _ll, _d, _vp, _sz, _vp]),
     "po_syrk_workspace_bytes": (_sz, [_ll, _ll, _i]),
-    "po_syrk_ema": (_i, [_vp, _ll, _ll, _vp, _i, _ll, _ll, _d, _d, _i, _vp, _sz, _vp]),
+    "po_syrk_ema": (_i, [_vp, _ll, _ll, _vp, _i, _ll, _ll, _d, _d, _i, _vp, _vp, _sz, _vp]),
     "po_precond_workspace_bytes": (_sz, [_ll, _ll, _i]),
     "po_precond_apply": (_i, [_vp, _ll, _vp, _ll, _vp, _ll, _vp, _ll, _i, _ll, _ll, _vp, _sz, _vp]),
     "po_precond_apply_norm": (_i, [_vp, _ll, _vp, _ll, _vp, _ll, _vp, _ll, _i, _ll, _ll, _vp, _vp, _sz, _vp]),

@@ -59,6 +59,20 @@ def _fingerprint(flags: list[str]) -> str:
     return h.hexdigest()
 
 
+def source_fingerprint(debug: bool = False) -> str:
+    """Short hash of every source, header and compiler flag of the library
+    (what a build of the current tree contains); profile summaries record it
+    so a figure taken from them can be matched to the build it describes."""
+    flags = ARCH_FLAGS + COMMON_FLAGS + (["-DPO_DEBUG=1"] if debug else [])
+    h = hashlib.sha256()
+    for p in _sources() + _headers():
+        with open(p, "rb") as f:
+            h.update(os.path.relpath(p, REPO_DIR).encode())
+            h.update(f.read())
+    h.update(" ".join(f for f in flags if not f.startswith(REPO_DIR)).encode())
+    return h.hexdigest()[:16]
+
+
 def build(force: bool = False, debug: bool = False, verbose: bool = False, jobs: int | None = None) -> str:
     """Compile every ``csrc/*.cu`` for sm_100a and link the shared library.
 

@@ -3,8 +3,10 @@
 //   Vt  = QG^T V QA
 //   S   = first ? Vt^2 : decay * S + (1 - decay) * Vt^2        (in place)
 //   out = QG (Vt / (S + lam)) QA^T
-// as four chained tensor-core products on split-bf16 operands (fp32-class
-// accuracy, like the two-sided apply). The second product's epilogue
+// as four chained tensor-core products on split-tf32 operands (hi*hi + hi*lo
+// + lo*hi on the tf32 tensor cores, ~2^-21 relative: fp32-grade, like the
+// two-sided apply; the division by S + lam amplifies operand rounding where
+// Vt is small, so bf16 pairs are not accurate enough). The second product's epilogue
 // updates S and writes Vt / (S + lam) straight into the operand pair of the
 // third, so Vt itself is never stored.
 #include "elementwise.cuh"
@@ -13,12 +15,12 @@
 namespace po {
 namespace {
 
-struct EkfacBufs {
-  __nv_bfloat16 *gh, *gl;  // QG  [m][m]
-  __nv_bfloat16 *ah, *al;  // QA  [n][n]
-  __nv_bfloat16 *vh, *vl;  // V   [m][n]
-  __nv_bfloat16 *th, *tl;  // QG^T V, then QG W  [m][n]
-  __nv_bfloat16 *wh, *wl;  // W = Vt / (S + lam)  [m][n]
+struct EkfacBufs {  // tf32 (hi, lo) pairs stored as fp32
+  float *gh, *gl;  // QG  [m][m]
+  float *ah, *al;  // QA  [n][n]
+  float *vh, *vl;  // V   [m][n]
+  float *th, *tl;  // QG^T V, then QG W  [m][n]
+  float *wh, *wl;  // W = Vt / (S + lam)  [m][n]
   long long ldm, ldn;
   unsigned int* sched;
 };
@@ -26,7 +28,7 @@ struct EkfacBufs {
 void ekfac_layout(Arena& ar, long long m, long long n, EkfacBufs& B) {
   B.ldm = round_up(m, 64);
   B.ldn = round_up(n, 64);
-  auto take = [&](long long elems) { return static_cast<__nv_bfloat16*>(ar.take(static_cast<size_t>(elems) * 2)); };
+  auto take = [&](long long elems) { return static_cast<float*>(ar.take(static_cast<size_t>(elems) * 4)); };
   B.gh = take(m * B.ldm);
   B.gl = take(m * B.ldm);
   B.ah = take(n * B.ldn);
@@ -40,10 +42,10 @@ void ekfac_layout(Arena& ar, long long m, long long n, EkfacBufs& B) {
   B.sched = take_sched(ar);
 }
 
-MatView bview(const __nv_bfloat16* p, long long rows, long long cols, long long ld) {
+MatView fview(const float* p, long long rows, long long cols, long long ld) {
   MatView v;
   v.ptr = p;
-  v.dtype = PO_BF16;
+  v.dtype = PO_F32;
   v.rows = rows;
   v.cols = cols;
   v.ld = ld;
@@ -51,11 +53,11 @@ MatView bview(const __nv_bfloat16* p, long long rows, long long cols, long long 
   return v;
 }
 
-// C = op(A) op(B) on split-bf16 pairs; epilogue set by the caller.
+// C = op(A) op(B) on split-tf32 pairs; epilogue set by the caller.
 GemmDesc split_product(const MatView (&a)[2], bool a_kmajor, const MatView (&b)[2], bool b_kmajor, long long M,
                        long long N, long long K, unsigned int* sched) {
   GemmDesc g;
-  g.kind = KIND_BF16;
+  g.kind = KIND_TF32;
   g.M = static_cast<int>(M);
   g.N = static_cast<int>(N);
   g.K = static_cast<int>(K);
@@ -66,7 +68,7 @@ GemmDesc split_product(const MatView (&a)[2], bool a_kmajor, const MatView (&b)[
   g.a_kmajor = a_kmajor;
   g.b_kmajor = b_kmajor;
   g.npass = 3;
-  g.chunked = 3 * K > 2048;
+  g.chunked = 3 * K > 1024;
   g.sched = sched;
   g.epi.alpha = 1.0f;
   return g;
@@ -105,18 +107,18 @@ extern "C" int po_ekfac_precondition(const float* QG, long long qg_ld, const flo
   if ((r = zero_sched(B.sched, s))) return r;
   AnyMat gm{QG, PO_F32, m, m, qg_ld, m * qg_ld}, am{QA, PO_F32, n, n, qa_ld, n * qa_ld},
       vm{V, PO_F32, m, n, v_ld, m * v_ld};
-  if ((r = launch_split_bf16(gm, 1, B.gh, B.gl, B.ldm, m * B.ldm, s))) return r;
-  if ((r = launch_split_bf16(am, 1, B.ah, B.al, B.ldn, n * B.ldn, s))) return r;
-  if ((r = launch_split_bf16(vm, 1, B.vh, B.vl, B.ldn, m * B.ldn, s))) return r;
-  const MatView QGv[2] = {bview(B.gh, m, m, B.ldm), bview(B.gl, m, m, B.ldm)};
-  const MatView QAv[2] = {bview(B.ah, n, n, B.ldn), bview(B.al, n, n, B.ldn)};
-  const MatView Vv[2] = {bview(B.vh, m, n, B.ldn), bview(B.vl, m, n, B.ldn)};
-  const MatView Tv[2] = {bview(B.th, m, n, B.ldn), bview(B.tl, m, n, B.ldn)};
-  const MatView Wv[2] = {bview(B.wh, m, n, B.ldn), bview(B.wl, m, n, B.ldn)};
-  auto split_out = [&](GemmDesc& g, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+  if ((r = launch_split_tf32(gm, 1, B.gh, B.gl, B.ldm, m * B.ldm, s))) return r;
+  if ((r = launch_split_tf32(am, 1, B.ah, B.al, B.ldn, n * B.ldn, s))) return r;
+  if ((r = launch_split_tf32(vm, 1, B.vh, B.vl, B.ldn, m * B.ldn, s))) return r;
+  const MatView QGv[2] = {fview(B.gh, m, m, B.ldm), fview(B.gl, m, m, B.ldm)};
+  const MatView QAv[2] = {fview(B.ah, n, n, B.ldn), fview(B.al, n, n, B.ldn)};
+  const MatView Vv[2] = {fview(B.vh, m, n, B.ldn), fview(B.vl, m, n, B.ldn)};
+  const MatView Tv[2] = {fview(B.th, m, n, B.ldn), fview(B.tl, m, n, B.ldn)};
+  const MatView Wv[2] = {fview(B.wh, m, n, B.ldn), fview(B.wl, m, n, B.ldn)};
+  auto split_out = [&](GemmDesc& g, float* hi, float* lo) {
     g.epi.nout = 2;
-    g.epi.out[0] = epi_out(hi, OUT_BF16, B.ldn, m * B.ldn);
-    g.epi.out[1] = epi_out(lo, OUT_BF16_LO, B.ldn, m * B.ldn);
+    g.epi.out[0] = epi_out(hi, OUT_TF32, B.ldn, m * B.ldn);
+    g.epi.out[1] = epi_out(lo, OUT_TF32_LO, B.ldn, m * B.ldn);
   };
 
   // T = QG^T V: A = QG stored [K = m][M = m] (MN-major), B = V [K = m][N = n] (MN-major).

@@ -328,4 +328,34 @@ int launch_split_bf16(const AnyMat& src, int batch, __nv_bfloat16* hi, __nv_bflo
   return check_cuda(cudaGetLastError(), "split launch");
 }
 
+// ------------------------------------------------------------- split tf32
+template <int DT>
+__global__ void split_tf32_kernel(AnyMat src, float* hi, float* lo, long long ld_dst, long long bs_dst) {
+  const int b = blockIdx.y;
+  for (long long r = blockIdx.x; r < src.rows; r += gridDim.x) {
+    const long long sb = b * src.bstride + r * src.ld, db = b * bs_dst + r * ld_dst;
+    for (long long c = threadIdx.x; c < src.cols; c += blockDim.x) {
+      const float v = static_cast<float>(Elem<DT>::ld(src.ptr, sb + c));
+      const float h = round_tf32(v);
+      hi[db + c] = h;
+      lo[db + c] = round_tf32(v - h);
+    }
+  }
+}
+
+int launch_split_tf32(const AnyMat& src, int batch, float* hi, float* lo, long long ld_dst, long long bs_dst,
+                      cudaStream_t s) {
+  if (src.rows <= 0 || src.cols <= 0 || batch <= 0) return PO_OK;
+  const int per = static_cast<int>(src.rows < 8LL * sm_count() ? src.rows : 8LL * sm_count());
+  dim3 grid(per, batch);
+  switch (src.dtype) {
+    case PO_F32: split_tf32_kernel<PO_F32><<<grid, 256, 0, s>>>(src, hi, lo, ld_dst, bs_dst); break;
+    case PO_BF16: split_tf32_kernel<PO_BF16><<<grid, 256, 0, s>>>(src, hi, lo, ld_dst, bs_dst); break;
+    case PO_F16: split_tf32_kernel<PO_F16><<<grid, 256, 0, s>>>(src, hi, lo, ld_dst, bs_dst); break;
+    case PO_F64: split_tf32_kernel<PO_F64><<<grid, 256, 0, s>>>(src, hi, lo, ld_dst, bs_dst); break;
+    default: return set_error(PO_ERR_ARG, "split: unsupported dtype");
+  }
+  return check_cuda(cudaGetLastError(), "split launch");
+}
+
 }  // namespace po

@@ -42,4 +42,11 @@ int launch_convert(const AnyMat& src, int batch, void* dst, int dst_dtype, long 
 int launch_split_bf16(const AnyMat& src, int batch, __nv_bfloat16* hi, __nv_bfloat16* lo, long long ld_dst,
                       long long bs_dst, cudaStream_t s);
 
+// Split a matrix batch into a tf32 pair (hi = tf32(x), lo = tf32(x - hi),
+// both stored as fp32, round to nearest): hi + lo carries ~22 significant
+// bits, and hi*hi + hi*lo + lo*hi on the tf32 tensor cores gives products
+// accurate to ~2^-21 (fp32-grade; the bf16 pair gives ~2^-16).
+int launch_split_tf32(const AnyMat& src, int batch, float* hi, float* lo, long long ld_dst, long long bs_dst,
+                      cudaStream_t s);
+
 }  // namespace po

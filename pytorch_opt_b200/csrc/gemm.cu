@@ -145,7 +145,8 @@ EpiOut epi_out(void* ptr, int out_kind, long long ld, long long bstride, bool tr
   e.ld = ld;
   e.bstride = bstride;
   e.trans = trans ? 1 : 0;
-  const int es = (out_kind == OUT_F32 || out_kind == OUT_TF32) ? 4 : (out_kind == OUT_F64 ? 8 : 2);
+  const int es = (out_kind == OUT_F32 || out_kind == OUT_TF32 || out_kind == OUT_TF32_LO) ? 4
+                 : (out_kind == OUT_F64 ? 8 : 2);
   e.vec = (reinterpret_cast<uintptr_t>(ptr) % 16 == 0) && (ld * es) % 16 == 0 && (bstride * es) % 16 == 0;
   return e;
 }

@@ -12,7 +12,9 @@
 //   "alpha*acc + sum(beta_i*C_i) + gamma*I" with up to three typed outputs,
 //   optional mirrored stores (symmetric products computed on the lower
 //   triangle of tiles only), an optional per-batch max|D - ident*I| or
-//   sum of D^2, the exact diagonal split, and the EKFAC rescaling.
+//   sum of D^2, the exact diagonal split (both operands' diagonals, or the
+//   left operand's as a per-row scale of the addend), the diagonal written
+//   out or summed (trace), and the EKFAC rescaling.
 // * Split-bf16 ("bf16x3") products: npass = 3 runs the K loop three times,
 //   hi*hi + hi*lo + lo*hi, into the same accumulator.
 //
@@ -37,6 +39,7 @@ enum OutKind : int {
   OUT_BF16_LO = 3,  // bf16(v - float(bf16(v))): low half of a split-bf16 pair
   OUT_F16 = 4,      // fp16
   OUT_F64 = 5,      // fp64 (scalar stores)
+  OUT_TF32_LO = 6,  // tf32(v - tf32(v)): low half of a split-tf32 pair
 };
 enum InKind : int { IN_F32 = 0, IN_BF16 = 1 };
 
@@ -96,6 +99,19 @@ struct Epilogue {
   // The addends are exactly symmetric (written by mirrored stores), so the
   // mirrored half of an off-diagonal tile takes the same values as the tile.
   int mirror_same;
+  // Row-diagonal split of a plain product U X whose left operand U reached
+  // the tensor cores with a zeroed diagonal, X being the addend in[0]: the
+  // epilogue adds u_i X_ij exactly, i.e. in[0] is scaled by
+  // beta + in0_rowcoef[b][i] instead of beta (nullable).
+  const float* in0_rowcoef;
+  long long in0_rowcoef_bs;
+  // Diagonal of the stored result: diag_out[b][i] = D_ii (nullable; written by
+  // the thread holding the diagonal element, on diagonal tiles).
+  float* diag_out;
+  long long diag_out_bs;
+  // Per batch: += sum of the stored diagonal values D_ii (nullable): the
+  // trace of the result, for KFAC's pi-split damping.
+  double* red_trace;
 };
 
 struct alignas(64) GemmParams {
@@ -182,10 +198,12 @@ __device__ __forceinline__ float bf16_lo(float v) {
   return v - hi;
 }
 
+__device__ __forceinline__ float tf32_lo(float v) { return round_tf32(v - round_tf32(v)); }
+
 // x[j] += beta * in(row, col0 + j) (columns >= ncols contribute 0).
-__device__ __forceinline__ void add_row(const EpiIn& in, int b, int row, int col0, int ncols, float (&x)[EC]) {
+__device__ __forceinline__ void add_row(const EpiIn& in, float beta, int b, int row, int col0, int ncols,
+                                        float (&x)[EC]) {
   const long long base = static_cast<long long>(b) * in.bstride + static_cast<long long>(row) * in.ld + col0;
-  const float beta = in.beta;
   if (in.kind == IN_F32) {
     const float* p = static_cast<const float*>(in.ptr) + base;
     if (in.vec && col0 + EC <= ncols) {
@@ -249,6 +267,7 @@ __device__ __forceinline__ void store_elem(const EpiOut& o, long long off, float
   switch (o.kind) {
     case OUT_F32: static_cast<float*>(o.ptr)[off] = v; break;
     case OUT_TF32: static_cast<float*>(o.ptr)[off] = round_tf32(v); break;
+    case OUT_TF32_LO: static_cast<float*>(o.ptr)[off] = tf32_lo(v); break;
     case OUT_BF16: static_cast<__nv_bfloat16*>(o.ptr)[off] = __float2bfloat16_rn(v); break;
     case OUT_BF16_LO: static_cast<__nv_bfloat16*>(o.ptr)[off] = __float2bfloat16_rn(bf16_lo(v)); break;
     case OUT_F64: static_cast<double*>(o.ptr)[off] = static_cast<double>(v); break;
@@ -284,6 +303,9 @@ __device__ __forceinline__ void store_row(const EpiOut& o, int b, int row, int c
         return;
       case OUT_TF32:
         store_row_f32x4(static_cast<float*>(o.ptr) + base, v, [](float x) { return round_tf32(x); });
+        return;
+      case OUT_TF32_LO:
+        store_row_f32x4(static_cast<float*>(o.ptr) + base, v, [](float x) { return tf32_lo(x); });
         return;
       case OUT_BF16:
         store_row_bf16x8(static_cast<__nv_bfloat16*>(o.ptr) + base, v, [](float x) { return x; });
@@ -324,6 +346,9 @@ __device__ __forceinline__ void store_col(const EpiOut& o, int b, int row, int c
       break;
     case OUT_TF32:
       store_col_typed(static_cast<float*>(o.ptr) + off, o.ld, nv, v, [](float x) { return round_tf32(x); });
+      break;
+    case OUT_TF32_LO:
+      store_col_typed(static_cast<float*>(o.ptr) + off, o.ld, nv, v, [](float x) { return tf32_lo(x); });
       break;
     case OUT_BF16:
       store_col_typed(static_cast<__nv_bfloat16*>(o.ptr) + off, o.ld, nv, v,
@@ -458,8 +483,13 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCo
       if (j == jd) v[j] += E.gamma;
   }
 #pragma unroll
-  for (int i = 0; i < kMaxEpiIn; ++i)
-    if (i < E.nin) add_row(E.in[i], tc.b, row, col0, N, v);
+  for (int i = 0; i < kMaxEpiIn; ++i) {
+    if (i < E.nin) {
+      float beta = E.in[i].beta;
+      if (i == 0 && E.in0_rowcoef != nullptr) beta += E.in0_rowcoef[static_cast<long long>(tc.b) * E.in0_rowcoef_bs + row];
+      add_row(E.in[i], beta, tc.b, row, col0, N, v);
+    }
+  }
   if (E.ek_s != nullptr) {
     float* sp = E.ek_s + static_cast<long long>(tc.b) * E.ek_bstride + static_cast<long long>(row) * E.ek_ld + col0;
 #pragma unroll
@@ -469,6 +499,15 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCo
         const float sn = E.ek_first ? sq : fmaf(1.0f - E.ek_decay, sq, sp[j] * E.ek_decay);  // s.mul_().add_()
         sp[j] = sn;
         v[j] = v[j] / (sn + E.ek_lam);                                           // Vt / (s + lam)
+      }
+    }
+  }
+  if ((E.diag_out != nullptr || E.red_trace != nullptr) && jd >= 0 && jd < EC && col0 + jd < N) {
+#pragma unroll
+    for (int j = 0; j < EC; ++j) {
+      if (j == jd) {
+        if (E.diag_out != nullptr) E.diag_out[static_cast<long long>(tc.b) * E.diag_out_bs + row] = v[j];
+        if (E.red_trace != nullptr) atomicAdd(E.red_trace + tc.b, static_cast<double>(v[j]));
       }
     }
   }

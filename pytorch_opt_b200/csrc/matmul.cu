@@ -12,19 +12,22 @@ struct Stored {
 };
 inline Stored stored(long long r, long long c, int trans) { return trans ? Stored{c, r} : Stored{r, c}; }
 
-// Staging area for one operand: 4 bytes per padded element, used either as
-// one fp32 / bf16 copy or as a bf16 (hi, lo) pair.
+// How an fp32 operand reaches the tensor cores.
+enum Split : int { SPLIT_NONE = 0, SPLIT_BF16 = 1, SPLIT_TF32 = 2 };
+
+// Staging area for one operand: 4 bytes per padded element (one fp32 / bf16
+// copy, or a bf16 (hi, lo) pair), 8 for a tf32 (hi, lo) pair.
 struct Staged {
   char* base;
   long long ld;
   long long elems;  // batch * rows * ld
 };
 
-inline Staged stage_layout(Arena& ar, long long batch, Stored st) {
+inline Staged stage_layout(Arena& ar, long long batch, Stored st, int bytes_per_elem) {
   Staged s;
   s.ld = round_up(st.cols, 64);
   s.elems = batch * st.rows * s.ld;
-  s.base = static_cast<char*>(ar.take(static_cast<size_t>(s.elems) * 4));
+  s.base = static_cast<char*>(ar.take(static_cast<size_t>(s.elems) * bytes_per_elem));
   return s;
 }
 
@@ -33,19 +36,30 @@ inline bool tma_ok(const void* p, long long ld, long long bs, long long batch, i
 }
 
 // Prepare operand views for the product (direct when aligned, else staged).
-// split: fp32 source turned into a bf16 (hi, lo) pair.
+// split: fp32 source turned into a bf16 or tf32 (hi, lo) pair.
 inline int prepare_operand(const void* X, int dtype, long long ld, long long bs, Stored st, long long batch,
-                           bool split, const Staged& stg, MatView out[2], cudaStream_t s) {
+                           int split, const Staged& stg, MatView out[2], cudaStream_t s) {
   AnyMat am{X, dtype, st.rows, st.cols, ld, bs};
-  if (split) {
-    __nv_bfloat16* hi = reinterpret_cast<__nv_bfloat16*>(stg.base);
-    __nv_bfloat16* lo = hi + stg.elems;
-    int r = launch_split_bf16(am, static_cast<int>(batch), hi, lo, stg.ld, st.rows * stg.ld, s);
+  if (split != SPLIT_NONE) {
+    const void* ps[2];
+    int r;
+    if (split == SPLIT_BF16) {
+      __nv_bfloat16* hi = reinterpret_cast<__nv_bfloat16*>(stg.base);
+      __nv_bfloat16* lo = hi + stg.elems;
+      r = launch_split_bf16(am, static_cast<int>(batch), hi, lo, stg.ld, st.rows * stg.ld, s);
+      ps[0] = hi;
+      ps[1] = lo;
+    } else {
+      float* hi = reinterpret_cast<float*>(stg.base);
+      float* lo = hi + stg.elems;
+      r = launch_split_tf32(am, static_cast<int>(batch), hi, lo, stg.ld, st.rows * stg.ld, s);
+      ps[0] = hi;
+      ps[1] = lo;
+    }
     if (r) return r;
-    const void* ps[2] = {hi, lo};
     for (int i = 0; i < 2; ++i) {
-      out[i].ptr = ps[i]; out[i].dtype = PO_BF16; out[i].rows = st.rows; out[i].cols = st.cols;
-      out[i].ld = stg.ld; out[i].bstride = st.rows * stg.ld;
+      out[i].ptr = ps[i]; out[i].dtype = split == SPLIT_BF16 ? PO_BF16 : PO_F32; out[i].rows = st.rows;
+      out[i].cols = st.cols; out[i].ld = stg.ld; out[i].bstride = st.rows * stg.ld;
     }
     return PO_OK;
   }
@@ -68,15 +82,15 @@ using namespace po;
 
 extern "C" size_t po_matmul_workspace_bytes(long long batch, long long M, long long N, long long K, int dtype,
                                             int precision) {
-  (void)dtype;
-  (void)precision;
   if (batch <= 0 || M <= 0 || N <= 0 || K <= 0) return 0;
+  const int per = (dtype == PO_F32 && precision == 2) ? 8 : 4;
   size_t best = 0;
   for (int ta = 0; ta < 2; ++ta)
     for (int tb = 0; tb < 2; ++tb) {
       Arena ar(nullptr, 0);
-      stage_layout(ar, batch, stored(M, K, ta));
-      stage_layout(ar, batch, stored(K, N, tb));
+      take_sched(ar);
+      stage_layout(ar, batch, stored(M, K, ta), per);
+      stage_layout(ar, batch, stored(K, N, tb), per);
       if (ar.used > best) best = ar.used;
     }
   return best + 256;
@@ -93,14 +107,18 @@ extern "C" int po_matmul(const void* A, long long lda, long long sa, int trans_a
   if (batch > 65535 || M > 0x3fffffff || N > 0x3fffffff || K > 0x3fffffff)
     return set_error(PO_ERR_ARG, "matmul: size too large");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (precision < 0 || precision > 2 || (precision == 2 && dtype != PO_F32))
+    return set_error(PO_ERR_ARG, "matmul: precision must be 0, 1 or 2 (2: fp32 operands only)");
   const Stored sta = stored(M, K, trans_a), stb = stored(K, N, trans_b);
+  const int split = dtype != PO_F32 ? SPLIT_NONE : (precision == 1 ? SPLIT_BF16 : (precision == 2 ? SPLIT_TF32
+                                                                                                    : SPLIT_NONE));
+  const int per = split == SPLIT_TF32 ? 8 : 4;
   Arena ar(workspace, workspace_bytes);
   unsigned int* sched = take_sched(ar);
-  const Staged ga = stage_layout(ar, batch, sta);
-  const Staged gb = stage_layout(ar, batch, stb);
+  const Staged ga = stage_layout(ar, batch, sta, per);
+  const Staged gb = stage_layout(ar, batch, stb, per);
   if (workspace == nullptr || ar.overflow()) return set_error(PO_ERR_WORKSPACE, "matmul: workspace too small");
 
-  const bool split = dtype == PO_F32 && precision == 1;
   GemmDesc g;
   g.M = static_cast<int>(M);
   g.N = static_cast<int>(N);
@@ -108,11 +126,11 @@ extern "C" int po_matmul(const void* A, long long lda, long long sa, int trans_a
   g.batch = static_cast<int>(batch);
   g.a_kmajor = !trans_a;  // A stored [M][K] is K-major
   g.b_kmajor = trans_b;   // B stored [N][K] is K-major
-  g.kind = (dtype == PO_BF16 || split) ? KIND_BF16 : KIND_TF32;
-  g.npass = split ? 3 : 1;
-  // The precise mode also sums K chunks outside the truncating accumulator
+  g.kind = (dtype == PO_BF16 || split == SPLIT_BF16) ? KIND_BF16 : KIND_TF32;
+  g.npass = split != SPLIT_NONE ? 3 : 1;
+  // The precise modes also sum K chunks outside the truncating accumulator
   // (for bf16 operands, precision 1 asks for that chunked accumulation alone).
-  g.chunked = precision == 1;
+  g.chunked = precision >= 1;
   g.sched = sched;
   int r;
   if ((r = zero_sched(sched, s))) return r;

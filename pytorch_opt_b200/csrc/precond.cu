@@ -2,15 +2,20 @@
 // (pytorch_opt/ops/reference.py:117-121; ATen version
 // pytorch_opt/ops/csrc/pytorch_opt_ops.cpp:96-99) as two chained tensor-core
 // products. The first product's epilogue writes L G directly as the operand
-// of the second (bf16 hi/lo pair for fp32 inputs, bf16 for bf16 inputs).
+// of the second. fp32 inputs run as split-tf32 pairs (hi = tf32(x),
+// lo = tf32(x - hi); hi*hi + hi*lo + lo*hi, ~2^-21 relative, fp32-grade:
+// Shampoo's eigh-route roots of rank-deficient factors carry entries of
+// order damping^(-1/4) whose products with G must stay accurate); bf16
+// inputs run as bf16 products.
 #include "elementwise.cuh"
 #include "gemm_host.cuh"
 
 namespace po {
 namespace {
 
+// Operand buffers: fp32 (hi, lo) pairs for fp32 inputs, bf16 (hi only) for bf16 inputs.
 struct PrecondBufs {
-  __nv_bfloat16 *lh, *ll, *gh, *gl, *rh, *rl, *ph, *pl;
+  void *lh, *ll, *gh, *gl, *rh, *rl, *ph, *pl;
   long long ldl, ldg, ldr;
   unsigned int* sched;  // tile queue of the two products
 };
@@ -19,7 +24,8 @@ void precond_layout(Arena& ar, long long m, long long n, bool split, PrecondBufs
   B.ldl = round_up(m, 64);
   B.ldg = round_up(n, 64);
   B.ldr = round_up(n, 64);
-  auto take = [&](long long elems) { return static_cast<__nv_bfloat16*>(ar.take(static_cast<size_t>(elems) * 2)); };
+  const size_t es = split ? 4 : 2;
+  auto take = [&](long long elems) { return ar.take(static_cast<size_t>(elems) * es); };
   B.lh = take(m * B.ldl);
   B.gh = take(m * B.ldg);
   B.rh = take(n * B.ldr);
@@ -31,15 +37,20 @@ void precond_layout(Arena& ar, long long m, long long n, bool split, PrecondBufs
   B.sched = take_sched(ar);
 }
 
-MatView bview(const __nv_bfloat16* p, long long rows, long long cols, long long ld) {
+MatView oview(const void* p, bool split, long long rows, long long cols, long long ld) {
   MatView v;
   v.ptr = p;
-  v.dtype = PO_BF16;
+  v.dtype = split ? PO_F32 : PO_BF16;
   v.rows = rows;
   v.cols = cols;
   v.ld = ld;
   v.bstride = rows * ld;
   return v;
+}
+
+int stage(const AnyMat& src, bool split, void* hi, void* lo, long long ld, cudaStream_t s) {
+  if (split) return launch_split_tf32(src, 1, static_cast<float*>(hi), static_cast<float*>(lo), ld, src.rows * ld, s);
+  return launch_split_bf16(src, 1, static_cast<__nv_bfloat16*>(hi), nullptr, ld, src.rows * ld, s);
 }
 
 }  // namespace
@@ -94,48 +105,49 @@ extern "C" int po_precond_apply_norm(const void* L, long long l_ld, const void* 
   int r;
   if ((r = zero_sched(B.sched, s))) return r;
   AnyMat lm{L, dtype, m, m, l_ld, m * l_ld}, gm{G, dtype, m, n, g_ld, m * g_ld}, rm{R, dtype, n, n, r_ld, n * r_ld};
-  if ((r = launch_split_bf16(lm, 1, B.lh, B.ll, B.ldl, m * B.ldl, s))) return r;
-  if ((r = launch_split_bf16(gm, 1, B.gh, B.gl, B.ldg, m * B.ldg, s))) return r;
-  if ((r = launch_split_bf16(rm, 1, B.rh, B.rl, B.ldr, n * B.ldr, s))) return r;
+  if ((r = stage(lm, split, B.lh, B.ll, B.ldl, s))) return r;
+  if ((r = stage(gm, split, B.gh, B.gl, B.ldg, s))) return r;
+  if ((r = stage(rm, split, B.rh, B.rl, B.ldr, s))) return r;
+  const int kind = split ? KIND_TF32 : KIND_BF16;
 
   // P = L G : A = L [m][m] (K-major), B = G stored [K = m][N = n] (MN-major).
   GemmDesc g1;
-  g1.kind = KIND_BF16;
+  g1.kind = kind;
   g1.M = static_cast<int>(m);
   g1.N = static_cast<int>(n);
   g1.K = static_cast<int>(m);
-  g1.a[0] = bview(B.lh, m, m, B.ldl);
-  g1.b[0] = bview(B.gh, m, n, B.ldg);
+  g1.a[0] = oview(B.lh, split, m, m, B.ldl);
+  g1.b[0] = oview(B.gh, split, m, n, B.ldg);
   if (split) {
-    g1.a[1] = bview(B.ll, m, m, B.ldl);
-    g1.b[1] = bview(B.gl, m, n, B.ldg);
+    g1.a[1] = oview(B.ll, split, m, m, B.ldl);
+    g1.b[1] = oview(B.gl, split, m, n, B.ldg);
     g1.npass = 3;
   }
   g1.b_kmajor = false;
   g1.sched = B.sched;
-  g1.chunked = split && 3 * m > 2048;
+  g1.chunked = split && 3 * m > 1024;
   g1.epi.alpha = 1.0f;
   g1.epi.nout = split ? 2 : 1;
-  g1.epi.out[0] = epi_out(B.ph, OUT_BF16, B.ldg, m * B.ldg);
-  if (split) g1.epi.out[1] = epi_out(B.pl, OUT_BF16_LO, B.ldg, m * B.ldg);
+  g1.epi.out[0] = epi_out(B.ph, split ? OUT_TF32 : OUT_BF16, B.ldg, m * B.ldg);
+  if (split) g1.epi.out[1] = epi_out(B.pl, OUT_TF32_LO, B.ldg, m * B.ldg);
   if ((r = launch_gemm(g1, s))) return r;
 
   // out = P R : A = P [m][n] (K-major), B = R stored [K = n][N = n] (MN-major).
   GemmDesc g2;
-  g2.kind = KIND_BF16;
+  g2.kind = kind;
   g2.M = static_cast<int>(m);
   g2.N = static_cast<int>(n);
   g2.K = static_cast<int>(n);
-  g2.a[0] = bview(B.ph, m, n, B.ldg);
-  g2.b[0] = bview(B.rh, n, n, B.ldr);
+  g2.a[0] = oview(B.ph, split, m, n, B.ldg);
+  g2.b[0] = oview(B.rh, split, n, n, B.ldr);
   if (split) {
-    g2.a[1] = bview(B.pl, m, n, B.ldg);
-    g2.b[1] = bview(B.rl, n, n, B.ldr);
+    g2.a[1] = oview(B.pl, split, m, n, B.ldg);
+    g2.b[1] = oview(B.rl, split, n, n, B.ldr);
     g2.npass = 3;
   }
   g2.b_kmajor = false;
   g2.sched = B.sched;
-  g2.chunked = split && 3 * n > 2048;
+  g2.chunked = split && 3 * n > 1024;
   g2.epi.alpha = 1.0f;
   g2.epi.nout = 1;
   g2.epi.out[0] = epi_out(out, dtype == PO_F32 ? OUT_F32 : OUT_BF16, out_ld, m * out_ld);

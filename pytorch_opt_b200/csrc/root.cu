@@ -24,7 +24,11 @@
 // adds the diagonal terms exactly (the accumulator truncates, which would
 // otherwise bias the many small off-diagonal terms summed next to one large
 // diagonal term). Convergence bookkeeping stays on the device; converged
-// batch items are skipped by later launches (no host sync).
+// batch items are skipped by later launches. Iterations are enqueued in
+// blocks of kIterBlock; after each block the host reads one 4-byte count of
+// items still iterating and stops enqueueing once it is zero (the reference
+// reads its error back after every iteration). Under stream capture no read
+// is possible, so all max_iter iterations are enqueued.
 #include <math.h>
 
 #include "elementwise.cuh"
@@ -34,6 +38,7 @@ namespace po {
 namespace {
 
 constexpr float kSplitUntil = 1e-3f;  // use split-bf16 products while err exceeds this
+constexpr int kIterBlock = 4;         // iterations enqueued between two reads of the active count
 
 struct Slot {
   float* f;
@@ -49,6 +54,7 @@ struct RootState {
   int* result;      // per batch: X slot holding the answer
   int* iters;       // per batch: steps taken
   double* sums;     // per batch: ||M||_F^2
+  int* count;       // items still active after the last block (read by the host)
 };
 
 struct RootBufs {
@@ -83,6 +89,7 @@ void root_layout(Arena& ar, long long batch, long long d, int p, RootBufs& B) {
   B.st.result = static_cast<int*>(ar.take(b * 4));
   B.st.iters = static_cast<int*>(ar.take(b * 4));
   B.st.sums = static_cast<double*>(ar.take(b * 8));
+  B.st.count = static_cast<int*>(ar.take(4));
   B.sched = take_sched(ar);
 }
 
@@ -182,6 +189,22 @@ __global__ void root_control(RootState st, int batch, int step, int p, float tol
   st.result[b] = (step + 1) & 1;
   if (err < tol || !(err == err)) st.active[b] = 0;
   st.passes[b] = err > kSplitUntil ? 3 : 1;
+}
+
+// st.count = number of batch items still iterating (one block).
+__global__ void root_count_active(RootState st, int batch) {
+  __shared__ int part[32];
+  int n = 0;
+  for (int b = threadIdx.x; b < batch; b += blockDim.x) n += st.active[b] != 0;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = n;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += part[w];
+    *st.count = t;
+  }
 }
 
 // out[b] = sym(X[result[b]][b]) cast to the output type.
@@ -307,6 +330,9 @@ extern "C" int po_inverse_root(const void* A, int dtype, long long batch, long l
 
   const float ftol = static_cast<float>(tol);
   const float inv_p = 1.0f / static_cast<float>(p);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if ((r = check_cuda(cudaStreamIsCapturing(s, &cap), "cudaStreamIsCapturing"))) return r;
+  const bool can_read = cap == cudaStreamCaptureStatusNone;
   for (int k = 0; k < max_iter; ++k) {
     const Slot& Dk = B.D[k & 1];
     const Slot& Dn = B.D[(k + 1) & 1];
@@ -344,6 +370,15 @@ extern "C" int po_inverse_root(const void* A, int dtype, long long batch, long l
     if (r) return r;
     root_control<<<cdiv(batch, 128), 128, 0, s>>>(B.st, nb, k, p, ftol);
     if ((r = check_cuda(cudaGetLastError(), "root control"))) return r;
+    if (can_read && (k + 1) % kIterBlock == 0 && k + 1 < max_iter) {
+      root_count_active<<<1, 256, 0, s>>>(B.st, nb);
+      if ((r = check_cuda(cudaGetLastError(), "root count"))) return r;
+      int active = 0;
+      if ((r = check_cuda(cudaMemcpyAsync(&active, B.st.count, sizeof(int), cudaMemcpyDeviceToHost, s), "count")))
+        return r;
+      if ((r = check_cuda(cudaStreamSynchronize(s), "root block sync"))) return r;
+      if (active == 0) break;
+    }
   }
 
   dim3 fgrid(cdiv(d, 32), cdiv(d, 32), nb);

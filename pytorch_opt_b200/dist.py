@@ -229,7 +229,7 @@ class ShardedMuon:
                                            self.layout.chunk_part(self.params_flat, self.rank, c),
                                            group=self.pg, async_op=True)
 
-    def _run(self, order_of_chunk, ns_events, before_group=None) -> None:
+    def _run(self, order_of_chunk, ns_events, before_group=None, tail_events=None) -> None:
         self._sq.zero_()
         pending = []
         for c in range(self.layout.chunks):
@@ -239,8 +239,15 @@ class ShardedMuon:
                 self._step_group(k, ns_events)
             if self.layout.world > 1:
                 pending.append(self._gather_chunk(c))
+        if tail_events is not None:  # after the last local kernel, before the wait for the last exchange
+            t0 = torch.cuda.Event(enable_timing=True)
+            t0.record()
         for w in pending:
             w.wait()
+        if tail_events is not None:
+            t1 = torch.cuda.Event(enable_timing=True)
+            t1.record()
+            tail_events.append((t0, t1))
 
     def _chunk_groups(self, c: int) -> list[int]:
         return [k for k, g in enumerate(self.layout.groups[self.rank]) if g.chunk == c]
@@ -258,9 +265,14 @@ class ShardedMuon:
         for w in [self._gather_chunk(c) for c in range(self.layout.chunks)]:
             w.wait()
 
-    def step(self, ns_events: list | None = None) -> None:
-        """Local update and exchange; chunk c's all-gather overlaps the update of chunks c+1.."""
-        self._run(self._chunk_groups, ns_events)
+    def step(self, ns_events: list | None = None, tail_events: list | None = None) -> None:
+        """Local update and exchange; chunk c's all-gather overlaps the update of chunks c+1..
+
+        ``tail_events``: optional list; a (start, end) pair of CUDA events is
+        appended that brackets the part of the step after this rank's last
+        kernel (the wait for the exchange still in flight: the exposed
+        communication)."""
+        self._run(self._chunk_groups, ns_events, tail_events=tail_events)
 
     def step_from_host(self, host_slot: torch.Tensor, ns_events: list | None = None) -> None:
         """One step whose gradients arrive from host memory.

@@ -13,7 +13,7 @@ This module exports exactly those, with the same argument meaning and the
 same error type for bad arguments (``RuntimeError``, as ``TORCH_CHECK``
 raises), implemented through the C ABI of ``libpytorch_opt_b200.so``. It is
 the object ``pytorch_opt.ops.native_build.load()`` returns once this package
-is plugged in. It serves CUDA tensors only: there is no
+is plugged in as the reference's native backend. It serves CUDA tensors only: there is no
 CPU code path here and no silent fallback.
 
 Extra entry points used by the optimizers' hot paths:
@@ -197,12 +197,15 @@ def precond_apply_grafted(L_root: torch.Tensor, G: torch.Tensor, R_root: torch.T
 # Extra hot-path entry points.
 # --------------------------------------------------------------------------
 
-def kron_syrk_ema_(F: torch.Tensor, X: torch.Tensor, alpha: float, beta: float, first: bool) -> torch.Tensor:
+def kron_syrk_ema_(F: torch.Tensor, X: torch.Tensor, alpha: float, beta: float, first: bool,
+                   trace: torch.Tensor | None = None) -> torch.Tensor:
     """In place: F <- alpha X^T X when ``first`` else beta F + (1 - beta) alpha X^T X.
 
     The KFAC factor statistic of ``pytorch_opt/curvature/kron.py:105-113``
     (A = a^T a / n: alpha = 1/n; G = ghat^T ghat / n with ghat = n g:
     alpha = n, applied to g) with the EMA of ``kron.py:95-103``.
+    ``trace``: optional fp64 CUDA scalar (a 0-d or 1-element view) that
+    receives tr(F) of the updated factor, summed by the product's epilogue.
     """
     dev = _require_cuda(F, X)
     if X.dim() != 2 or F.dim() != 2 or F.shape[0] != F.shape[1] or F.shape[0] != X.shape[1]:
@@ -216,8 +219,13 @@ def kron_syrk_ema_(F: torch.Tensor, X: torch.Tensor, alpha: float, beta: float, 
         code = _lib.DTYPE_CODE[Xw.dtype]
         nbytes = lib.po_syrk_workspace_bytes(rows, d, code)
         ws = _lib.workspace(nbytes, dev)
+        tptr = None
+        if trace is not None:
+            if trace.dtype != torch.float64 or not trace.is_cuda or trace.numel() != 1:
+                raise RuntimeError("kron_syrk_ema_: trace must be a one-element fp64 CUDA tensor")
+            tptr = trace.data_ptr()
         _call("po_syrk_ema", F.data_ptr(), d, d, Xw.data_ptr(), code, rows, d, float(alpha), float(beta),
-              1 if first else 0, ws.data_ptr(), nbytes, _lib.stream_ptr(dev))
+              1 if first else 0, tptr, ws.data_ptr(), nbytes, _lib.stream_ptr(dev))
     return F
 
 
@@ -228,6 +236,86 @@ def damped_inverse(F: torch.Tensor, gamma: float, max_iter: int = 100, tol: floa
     ``pytorch_opt/optim/kfac.py:134-138``.
     """
     return inverse_matrix_root(F, 1, gamma, "newton", True, max_iter, tol)
+
+
+def kfac_factored_damping(A: torch.Tensor, G: torch.Tensor, damping: float,
+                          traces: torch.Tensor | None = None) -> tuple[float, float]:
+    """KFAC's pi-split of the damping (``pytorch_opt/curvature/damping.py:10-25``).
+
+    pi = sqrt((tr(A)/dim A) / (tr(G)/dim G)) (pi = 1 when either mean is not
+    finite and positive); returns (pi sqrt(damping), sqrt(damping) / pi).
+    ``traces``: optional fp64 CUDA tensor [tr(A), tr(G)], e.g. written by
+    ``kron_syrk_ema_(..., trace=traces[0])``; otherwise both diagonals are
+    summed on the device. Either way the host reads the two traces once (the
+    reference reads each with its own ``float()``).
+    """
+    if traces is None:
+        traces = torch.stack([A.diagonal(dim1=-2, dim2=-1).sum().double(), G.diagonal(dim1=-2, dim2=-1).sum().double()])
+    tr_a, tr_g = traces.tolist()
+    nu_a = tr_a / A.shape[-1]
+    nu_g = tr_g / G.shape[-1]
+    if not (math.isfinite(nu_a) and math.isfinite(nu_g)) or nu_a <= 0 or nu_g <= 0:
+        pi = 1.0
+    else:
+        pi = math.sqrt(nu_a / nu_g)
+    sq = math.sqrt(damping)
+    return pi * sq, sq / pi
+
+
+class _no_tf32:
+    """fp32 torch products without TF32 inside the block."""
+
+    def __enter__(self):
+        self.old = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+
+    def __exit__(self, *exc):
+        torch.backends.cuda.matmul.allow_tf32 = self.old
+
+
+def _top_eigenvalue(F: torch.Tensor, block: int = 16, steps: int = 16, seed: int = 0) -> float:
+    """Largest eigenvalue of a symmetric matrix by block Krylov (Rayleigh-Ritz
+    on span{Q, FQ, ..., F^(steps-1) Q}, Q a seeded random d x block block):
+    a lower bound within ~1e-4 relative of the exact value on the spectra of
+    KFAC factors (dense Marchenko-Pastur-like edges)."""
+    d = F.shape[-1]
+    Ff = F.float()
+    g = torch.Generator(device=F.device).manual_seed(seed)
+    Q = torch.linalg.qr(torch.randn(d, block, generator=g, device=F.device))[0]
+    basis = [Q]
+    with _no_tf32():
+        for _ in range(steps - 1):
+            W = Ff @ basis[-1]
+            Qa = torch.cat(basis, 1)
+            W = W - Qa @ (Qa.mT @ W)
+            W = W - Qa @ (Qa.mT @ W)  # second pass keeps the basis orthogonal in fp32
+            basis.append(torch.linalg.qr(W)[0])
+        Qa = torch.cat(basis, 1)
+        T = (Qa.mT @ (Ff @ Qa)).double()
+    return float(torch.linalg.eigvalsh(0.5 * (T + T.mT)).max())
+
+
+def kfac_damped_inverse(F: torch.Tensor, gamma: float, max_iter: int = 100,
+                        tol: float = 1e-10) -> tuple[torch.Tensor, float]:
+    """``KFAC._damped_inverse`` (``pytorch_opt/optim/kfac.py:134-138``): returns
+    ``((F + gamma I)^-1, cond)`` with cond = (lambda_max + gamma) /
+    (lambda_min + gamma), F's dtype kept.
+
+    The inverse is the tensor-core coupled Newton iteration with p = 1
+    (``damped_inverse``). The reference takes both from an fp64 ``eigh``;
+    here cond = ||F + gamma I||_2 * ||inverse||_2 with both spectral norms
+    from block Krylov on the device (exact ``eigvalsh`` for d <= 512), one
+    host read.
+    """
+    inv = damped_inverse(F, gamma, max_iter, tol)
+    d = F.shape[-1]
+    if d <= 512:
+        ev = torch.linalg.eigvalsh(F.double())
+        lo, hi = ev.min() + gamma, ev.max() + gamma
+        cond = float(hi / lo.clamp_min(1e-300))
+    else:
+        cond = (_top_eigenvalue(F) + gamma) * _top_eigenvalue(inv)
+    return inv.to(F.dtype), cond
 
 
 def newton_schulz_batched(Gs, steps: int = 5, coeffs=(3.4445, -4.7750, 2.0315), eps: float = 1e-7):

@@ -5,9 +5,10 @@ turn with ``PO_GEMM_PAIR``, on all four operand layouts, both operand kinds,
 ragged shapes (partial tiles in M, N and K) and batches.
 
 Reference: float64 matmul of the operands as the tensor cores see them
-(bf16 exactly; fp32 inputs rounded to tf32 by truncation for precision 0).
-Tolerances, relative Frobenius: bf16 and split-bf16 2e-5 (fp32 accumulation
-over K <= 1100), tf32 2e-3 (10-bit mantissa operands).
+(bf16 exactly; fp32 inputs rounded to tf32 by truncation for precision 0,
+exact for the split precisions 1 and 2). Tolerances, relative Frobenius:
+bf16 and split-bf16 2e-5 (fp32 accumulation over K <= 1100), split-tf32
+2e-6, tf32 2e-3 (10-bit mantissa operands).
 """
 
 import ctypes
@@ -48,8 +49,8 @@ def _matmul(A, B, C, ta, tb, precision, alpha, beta):
 
 
 def _reference(A, B, C0, ta, tb, precision, alpha, beta):
-    a = A.double() if A.dtype == torch.bfloat16 or precision == 1 else _tf32_trunc(A).double()
-    b = B.double() if B.dtype == torch.bfloat16 or precision == 1 else _tf32_trunc(B).double()
+    a = A.double() if A.dtype == torch.bfloat16 or precision >= 1 else _tf32_trunc(A).double()
+    b = B.double() if B.dtype == torch.bfloat16 or precision >= 1 else _tf32_trunc(B).double()
     if ta:
         a = a.transpose(1, 2)
     if tb:
@@ -62,7 +63,10 @@ def _rel(x, y):
 
 
 LAYOUTS = [(0, 0), (0, 1), (1, 0), (1, 1)]
-KINDS = [(torch.bfloat16, 0, 2e-5), (torch.float32, 0, 2e-3), (torch.float32, 1, 2e-5)]
+# (bf16, 1): bf16 products whose K is summed in chunks outside the accumulator;
+# (fp32, 1): split-bf16 pairs; (fp32, 2): split-tf32 pairs (fp32-grade).
+KINDS = [(torch.bfloat16, 0, 2e-5), (torch.bfloat16, 1, 2e-5), (torch.float32, 0, 2e-3), (torch.float32, 1, 2e-5),
+         (torch.float32, 2, 2e-6)]
 
 
 @pytest.mark.parametrize("pair", ["0", "1"])

@@ -132,3 +132,69 @@ def test_ekfac_oracle_matches_reference_golden():
             want = z[f"case{i}_{key}"]
             assert np.linalg.norm(got - want) / np.linalg.norm(want) <= 1e-5, (i, key)
 
+
+
+# --------------------------------------------------- torch full-size checker
+# oracle/ops_torch.py evaluates the same algorithms with torch (on the GPU in
+# the full-size parity tests); here it is pinned on the CPU to the same
+# golden vectors as the numpy restatement.
+
+def test_torch_checker_newton_schulz_golden():
+    import torch
+    from oracle import ops_torch as T
+    z = _load("ns.npz")
+    for i in range(int(z["ncases"])):
+        x, want, (steps, dt) = z[f"case{i}_in"], z[f"case{i}_out"], z[f"case{i}_meta"]
+        G = torch.from_numpy(x).to({0: torch.float32, 1: torch.bfloat16, 3: torch.float64}[int(dt)])
+        got = T.newton_schulz(G, int(steps)).double().numpy()
+        tol = {0: 1e-5, 1: 2e-3, 3: 1e-12}[int(dt)]
+        assert _rel(got, want) < tol, (i, _rel(got, want))
+
+
+def test_torch_checker_newton_roots_golden():
+    import torch
+    from oracle import ops_torch as T
+    z = _load("roots.npz")
+    for i in range(int(z["ncases"])):
+        A, want, (p, damping, m) = z[f"case{i}_in"], z[f"case{i}_out"], z[f"case{i}_meta"]
+        if ("auto", "eigh", "newton")[int(m)] != "newton" or A.ndim != 2:
+            continue
+        X, its = T.inverse_root_newton(torch.from_numpy(A), int(p), float(damping))
+        _, its_np = O.coupled_newton(0.5 * (A + A.T).astype(np.float64) + float(damping) * np.eye(A.shape[0]), int(p))
+        assert its == its_np
+        assert _rel(X.numpy().astype(A.dtype), want) < (1e-10 if A.dtype == np.float64 else 1e-6), i
+
+
+def test_torch_checker_kfac_golden():
+    import torch
+    from oracle import ops_torch as T
+    z = _load("kfac.npz")
+    for i in range(int(z["ncases"])):
+        bias, ema = z[f"case{i}_meta"]
+        if ema < 0:
+            continue
+        FA = FG = None
+        for step in range(3):
+            a = torch.from_numpy(z[f"case{i}_a{step}"])
+            g = torch.from_numpy(z[f"case{i}_g{step}"])
+            n = a.shape[0]
+            if bias:
+                a = torch.cat([a, torch.ones(n, 1)], dim=1)
+            FA = T.kfac_update(FA, T.kron_batch_factor(a, 1.0 / n), float(ema))
+            FG = T.kfac_update(FG, T.kron_batch_factor(g, float(n)), float(ema))
+        assert _rel(FA.numpy(), z[f"case{i}_A"]) < 1e-6 and _rel(FG.numpy(), z[f"case{i}_G"]) < 1e-6
+        ga, gg = z[f"case{i}_gammas"]
+        iA, cA = T.damped_inverse(torch.from_numpy(z[f"case{i}_A"]), float(ga))
+        iG, cG = T.damped_inverse(torch.from_numpy(z[f"case{i}_G"]), float(gg))
+        assert _rel(iA.numpy(), z[f"case{i}_iA"]) < 1e-6 and _rel(iG.numpy(), z[f"case{i}_iG"]) < 1e-6
+        np.testing.assert_allclose([cA, cG], z[f"case{i}_conds"], rtol=1e-10)
+
+
+def test_full_size_fixture_is_complete():
+    """The full-size fixture holds what the GPU tests read, and the reference's
+    iteration counts on config 3 (d = 1024 / 2048 / 4096)."""
+    z = _load("full_size.npz")
+    for i in range(4):
+        assert z[f"ns{i}_sketch"].shape == (32, 32)
+    assert [int(z[f"root{d}_iters"]) for d in (1024, 2048, 4096)] == [10, 11, 11]
+    assert z["kfac_iA_sketch"].shape == (32, 32) and z["kfac_conds"].shape == (2,)

@@ -6,19 +6,25 @@ that is handed device pointers but no allocator. ``po_newton_schulz_static``
 serves them from a fixed scratch array inside the library. These tests call
 it through the C ABI twice in a row (the scratch keeps the previous call's
 contents) and compare each result with the workspace-taking
-``po_newton_schulz`` on the same input, within the Newton–Schulz tolerance
-used by the parity tests. They also check that a problem larger than the
-scratch is refused with a clear error. This file is collected last.
+``po_newton_schulz`` on the same input: both run the same kernels, so they
+must agree to 1e-6 (the per-matrix norm is summed with atomics, whose order
+may move its last bits). Each result is also checked against the numpy
+oracle within the Newton–Schulz tolerance of the parity tests (1e-2
+relative Frobenius). A problem larger than the scratch must be refused with
+a clear error. This file is collected last.
 """
 
+import numpy as np
 import pytest
 import torch
 
+from oracle import ops_np as O
 from pytorch_opt_b200 import _lib
 
 pytestmark = pytest.mark.gpu
 
 NS_TOL = 1e-2
+SAME_KERNELS_TOL = 1e-6
 COEFFS = (3.4445, -4.7750, 2.0315)
 CODE = {torch.float32: 0, torch.bfloat16: 1}
 
@@ -58,8 +64,12 @@ def test_static_scratch_matches_workspace_entry_twice(cuda):
         assert rc == 0, _lib.last_error()
         want = _with_workspace(G)
         torch.cuda.synchronize(cuda)
-        assert _rel(got, want) <= NS_TOL
+        assert _rel(got, want) <= SAME_KERNELS_TOL, _rel(got, want)
         assert torch.isfinite(got.float()).all()
+        x = G.float().cpu().numpy()
+        oracle = O.newton_schulz(x, 5, out_bf16=(G.dtype == torch.bfloat16))
+        got64 = got.double().cpu().numpy()
+        assert np.linalg.norm(got64 - oracle) / np.linalg.norm(oracle) <= NS_TOL
     assert _lib.device_error(reset=True) == 0
 
 
