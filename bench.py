@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the B200-native pytorch_opt.ops hot path.
 
-Default workload: one Muon step over the Llama-3-8B
+Default workload (configuration 5): one Muon step over the Llama-3-8B
 matrix parameters — 32 layers x {q, o: 4096x4096; k, v: 1024x4096;
 gate, up: 14336x4096; down: 4096x14336} = 224 bf16 matrices, grads
 0.02*N(0,1), momentum 0.95 Nesterov, 5 Newton–Schulz steps, weight decay 0,
@@ -11,10 +11,16 @@ time; 665.9 TFLOP of dense Newton–Schulz work per step.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Prints one JSON line on rank 0. ``--impl reference`` times the reference's
-own CPU implementation (its ATen extension compiled under ``oracle/_ref``,
-else the numpy restatement) on this host's cores over a bounded sample of the
-same step, scaled to the full step by FLOPs.
+Prints one JSON line on rank 0. At N = 1 the line also carries the same
+Newton-Schulz work through torch/cuBLAS on the GPU (``gpu_library_bar``),
+configurations 1-4 of the benchmark suite (``secondary``, each with its clocks and
+CPU baseline) and the reference's CPU time per distinct shape
+(``cpu_baseline``); at N > 1 a ``scaling_detail`` object (per-rank compute and
+exposed exchange time, LPT imbalance). ``--impl reference`` times the
+reference's own CPU implementation (its ATen extension compiled under
+``oracle/_ref``, else the numpy restatement) on this host's cores: every
+timed step is one sampled matrix, cycling the four distinct shapes, and the
+full-step value is built from the per-shape sample times.
 """
 
 from __future__ import annotations
@@ -36,17 +42,37 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 
 LLAMA_LAYER = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096), (14336, 4096), (4096, 14336)]
+LLAMA_DISTINCT = [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336)]
+LLAMA_COUNT = {s: 32 * LLAMA_LAYER.count(s) for s in LLAMA_DISTINCT}
 METRIC = "Muon NS5 step ms (8B shapes)"
 MEASURED_PEAKS = os.path.join(HERE, "MEASURED_PEAKS.json")
 
 
 
-# DRAM traffic (ncu dram__bytes_read.sum + dram__bytes_write.sum, summed over
-# the Newton-Schulz product launches) of the two captured workloads; the
-# commands and per-kernel figures are in profiles/launches_llama8b_muon_step.md
-# and profiles/tc_gemm_pair_ns4096.md.
-LLAMA_STEP_TRAFFIC = 1_120_000_000_000   # bytes per 1-GPU step (808.5 GB read + 311.5 GB write)
-NS4096_CALL_TRAFFIC = 13_660_000_000     # bytes per NS5 call on 4 x 4096^2 (9.65 GB read + 4.01 GB write)
+PROFILES = os.path.join(HERE, "profiles")
+
+
+def profiled_traffic(summary: str):
+    """DRAM bytes recorded in a committed ncu summary under profiles/.
+
+    The summary carries one line ``bench-traffic: <bytes> bytes; source
+    <fingerprint>``: ncu's dram__bytes_read.sum + dram__bytes_write.sum of the
+    workload's product launches, and the library source fingerprint of the
+    build that was profiled. Returns (bytes or None, profiled fingerprint,
+    whether it equals the current tree's)."""
+    from pytorch_opt_b200.build import source_fingerprint
+    try:
+        with open(os.path.join(PROFILES, summary)) as f:
+            for line in f:
+                if line.startswith("bench-traffic:"):
+                    parts = line.split()
+                    nbytes = int(parts[1])
+                    fp = parts[parts.index("source") + 1] if "source" in parts else None
+                    return nbytes, fp, fp == source_fingerprint()
+    except (OSError, ValueError, IndexError):
+        pass
+    return None, None, False
+
 
 def llama_shapes():
     return LLAMA_LAYER * 32
@@ -123,63 +149,97 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------- CPU baseline
-def cpu_reference_sample(reps: int = 2, warm: int = 1):
-    """Time the reference's CPU NS5 on one 4096x4096 bf16 matrix (a q/o projection).
-
-    Returns (seconds per sample, kind, threads, description).
-    """
-    threads = len(os.sched_getaffinity(0))
-    torch.set_num_threads(threads)
-    g = torch.Generator().manual_seed(1000)
-    G = (torch.randn(4096, 4096, generator=g) * 0.02).bfloat16()
-    kind, fn = "port", None
+def _ref_ns_fn():
+    """The reference's NS5 on the CPU: its own ATen extension (compiled under
+    oracle/_ref) when present, else the numpy restatement. Returns
+    (callable(G) -> None, kind, description of the implementation)."""
     try:
         from oracle import ref_native
         mod = ref_native.load()
-        if mod is not None:
-            kind = "reference"
-            fn = lambda: mod.newton_schulz_orthogonalize(G, 5, 3.4445, -4.7750, 2.0315, 1e-7)  # noqa: E731
     except Exception:
-        fn = None
-    if fn is None:
-        from oracle import ops_np
-        Gn = G.float().numpy()
-        fn = lambda: ops_np.newton_schulz(Gn, 5, out_bf16=True)  # noqa: E731
-    for _ in range(warm):
-        fn()
-    ts = []
-    for _ in range(reps):
+        mod = None
+    if mod is not None:
+        return (lambda G: mod.newton_schulz_orthogonalize(G, 5, 3.4445, -4.7750, 2.0315, 1e-7), "reference",
+                "the reference's own ATen extension (pytorch_opt_ops.cpp:65-81, compiled under oracle/_ref)")
+    from oracle import ops_np
+    return (lambda G: ops_np.newton_schulz(G.float().numpy(), 5, out_bf16=True), "port",
+            "the reference algorithm restated in numpy (oracle/ops_np.py)")
+
+
+def _llama_sample(shape, seed):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * 0.02).bfloat16()
+
+
+def cpu_reference_per_shape():
+    """One NS5 of each distinct Llama-3-8B shape by the reference's CPU path
+    (all host threads), summed by multiplicity into a full-step estimate."""
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    fn, kind, impl = _ref_ns_fn()
+    per = {}
+    for i, shape in enumerate(LLAMA_DISTINCT):
+        G = _llama_sample(shape, 1000 + i)
+        if i == 0:
+            fn(G)  # warm-up (thread pools, first-touch)
         t0 = time.perf_counter()
-        fn()
-        ts.append(time.perf_counter() - t0)
-    desc = ("NS5 of one 4096x4096 bf16 matrix (q/o shape) by the reference's own "
-            + ("ATen extension (pytorch_opt_ops.cpp, compiled under oracle/_ref)" if kind == "reference"
-               else "algorithm restated in numpy (oracle/ops_np.py)")
-            + f", median of {reps}, scaled to the 224-matrix step by dense FLOPs")
-    return statistics.median(ts), kind, threads, desc
+        fn(G)
+        per[shape] = (time.perf_counter() - t0) * 1e3
+    total = sum(LLAMA_COUNT[s] * per[s] for s in LLAMA_DISTINCT)
+    desc = (f"one NS5 per distinct shape by {impl}, bf16 0.02 N(0,1) inputs, {threads} threads; "
+            "full step = sum over shapes of multiplicity x time")
+    return total, per, kind, threads, desc
 
 
 def run_reference_arm(args, rank, world):
-    """--impl reference: the reference's CPU path, rank 0 only."""
+    """--impl reference: the reference's CPU path on this host, rank 0 only.
+
+    A full Llama-3-8B step takes minutes of CPU time per matrix group, so each
+    timed "step" here is one sampled matrix: the four distinct shapes are
+    cycled (4096^2, 1024x4096, 14336x4096, 4096x14336), every sample timed,
+    and the full-step value is the sum over shapes of multiplicity x the
+    shape's median sample time. ms_per_step is the mean measured sample time,
+    so ms_per_step x steps is the time actually spent in the timed region.
+    """
     if rank != 0:
         return 0
-    total = sum(ns_flops(r, c) for r, c in llama_shapes())
-    sample = ns_flops(4096, 4096)
-    times = []
-    kind = threads = desc = None
-    for i in range(args.warmup + args.steps):
-        t, kind, threads, desc = cpu_reference_sample(reps=1, warm=0)
-        if i >= args.warmup:
-            times.append(t * total / sample * 1e3)
-    ms = statistics.median(times)
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    fn, kind, impl = _ref_ns_fn()
+    inputs = [_llama_sample(s, 1000 + i) for i, s in enumerate(LLAMA_DISTINCT)]
+    for i in range(args.warmup):
+        fn(inputs[i % len(inputs)])
+    samples = {s: [] for s in LLAMA_DISTINCT}
+    t_all = time.perf_counter()
+    for i in range(args.steps):
+        j = i % len(inputs)
+        t0 = time.perf_counter()
+        fn(inputs[j])
+        samples[LLAMA_DISTINCT[j]].append((time.perf_counter() - t0) * 1e3)
+    timed_ms = (time.perf_counter() - t_all) * 1e3
+    per = {}
+    for s in LLAMA_DISTINCT:
+        if samples[s]:
+            per[s] = statistics.median(samples[s])
+    # Shapes not sampled (steps < 4) are scaled from the sampled ones by dense FLOPs.
+    rate = sum(ns_flops(*s) for s in per) / sum(per.values())
+    for s in LLAMA_DISTINCT:
+        per.setdefault(s, ns_flops(*s) / rate)
+    value = sum(LLAMA_COUNT[s] * per[s] for s in LLAMA_DISTINCT)
+    sample_desc = (f"{args.steps} timed samples cycling the 4 distinct Llama-3-8B shapes, one NS5 each by {impl}, "
+                   f"{threads} threads; value = sum over shapes of multiplicity x median sample time")
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(ms, 3), "unit": "ms", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False,
-        "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": "ms", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(timed_ms / args.steps, 3),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
         "config": {"workload": "Muon NS5 step over Llama-3-8B matrix params (224 matrices)", "ns_steps": 5,
-                   "parallelism": "host CPU, all threads"},
-        "cpu_baseline": {"value": round(ms, 3), "unit": "ms", "cores": threads, "kind": kind, "sample": desc},
-        "e2e": {"value": round(ms, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                   "parallelism": "host CPU, all threads",
+                   "sampled": {"per_shape_ms": {f"{r}x{c}": round(per[(r, c)], 2) for r, c in LLAMA_DISTINCT},
+                               "multiplicity": {f"{r}x{c}": LLAMA_COUNT[(r, c)] for r, c in LLAMA_DISTINCT},
+                               "note": "each step is one sampled matrix; ms_per_step is the mean sample time, "
+                                       "value the full 224-matrix step built from the samples"}},
+        "cpu_baseline": {"value": round(value, 1), "unit": "ms", "cores": threads, "kind": kind, "sample": sample_desc},
+        "e2e": {"value": round(value, 1), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -189,6 +249,53 @@ def run_reference_arm(args, rank, world):
 def fill_normal(t: torch.Tensor, seed: int, scale: float):
     g = torch.Generator(device=t.device).manual_seed(seed)
     t.copy_(torch.randn(t.shape, generator=g, device=t.device, dtype=torch.float32).mul_(scale))
+
+
+def _torch_ns(G: torch.Tensor, dt: torch.dtype) -> torch.Tensor:
+    """NS5 as torch ops in dtype dt: the op sequence of the reference's ATen
+    module (pytorch_opt_ops.cpp:65-81; fp32 work dtype) when dt is fp32."""
+    a, b, c = 3.4445, -4.7750, 2.0315
+    X = G.to(dt)
+    tall = X.shape[-2] > X.shape[-1]
+    if tall:
+        X = X.mT
+    X = X / (X.float().norm() + 1e-7).to(dt)
+    for _ in range(5):
+        A = X @ X.mT
+        B = b * A + c * (A @ A)
+        X = a * X + B @ X
+    if tall:
+        X = X.mT
+    return X.to(G.dtype)
+
+
+def gpu_library_bar(mats: list, dev: torch.device) -> dict:
+    """The same Newton-Schulz work through torch/cuBLAS on this GPU, one matrix
+    at a time as the reference's Muon loop calls it (muon.py:70-98): fp32
+    SGEMM (TF32 off; the reference's ATen path on CUDA tensors) over one full
+    224-matrix step, and the same chain on bf16 matmuls (a speed bar only: an
+    all-bf16 chain misses the 1e-2 tolerance)."""
+    old = torch.backends.cuda.matmul.allow_tf32
+    out = {}
+    try:
+        for name, dt, reps in (("torch_fp32_cublas_ms", torch.float32, 1), ("torch_bf16_cublas_ms", torch.bfloat16, 2)):
+            torch.backends.cuda.matmul.allow_tf32 = False
+            for shape in LLAMA_DISTINCT:  # warm-up: one matrix of each shape
+                _torch_ns(next(m for m in mats if tuple(m.shape) == shape), dt)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                for m in mats:
+                    _torch_ns(m, dt)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            out[name] = round(e0.elapsed_time(e1) / reps, 1)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old
+    out["how"] = ("torch ops per matrix (cast, transpose if tall, normalise, 5 x 3 matmuls, cast back), CUDA-event "
+                  "time of one full step (fp32) / mean of two (bf16), inputs resident")
+    return out
 
 
 def run_ours(args, rank, world, local_rank):
@@ -219,12 +326,13 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    def max_over_ranks(x: float) -> float:
+    def all_ranks(x: float) -> list:
         if world == 1:
-            return x
+            return [x]
         t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        out = torch.empty(world, dtype=torch.float64, device=dev)
+        dist.all_gather_into_tensor(out, t)
+        return out.tolist()
 
     # ---------------------------------------------------- device-resident run
     for _ in range(args.warmup):
@@ -233,16 +341,21 @@ def run_ours(args, rank, world, local_rank):
     clocks = ClockSampler(dev)
     clocks.start()
     ns_events: list = []
+    tail_events: list = []
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        sm.step(ns_events)
+        sm.step(ns_events, tail_events)
     e1.record(stream)
     barrier()
     clk = clocks.stop()
-    step_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    step_ranks = all_ranks(e0.elapsed_time(e1) / args.steps)
+    step_ms = max(step_ranks)
     ns_ms_local = sum(a.elapsed_time(b) for a, b in ns_events) / args.steps
-    gemm_tflops_local = local_flops / (ns_ms_local * 1e-3) / 1e12 if ns_ms_local > 0 else 0.0
+    tail_ms_local = sum(a.elapsed_time(b) for a, b in tail_events) / args.steps
+    ns_ranks = all_ranks(ns_ms_local)
+    tail_ranks = all_ranks(tail_ms_local)
+    gemm_tflops = min(all_ranks(local_flops / (ns_ms_local * 1e-3) / 1e12 if ns_ms_local > 0 else 0.0))
     launches = sm.launches_per_step() * args.steps
 
     # -------------------------------------------------------------- e2e run
@@ -258,35 +371,45 @@ def run_ours(args, rank, world, local_rank):
         a0.record(stream)
         for _ in range(args.steps):
             sm.step_from_host(host)                   # this step's gradients, from pinned host memory
-
             sq.copy_(sm._sq.sum().reshape(1))
             if world > 1:
                 dist.all_reduce(sq)
             _ = float(sq.item())                      # the step's diagnostic, read back on the host
         a1.record(stream)
         barrier()
-        e2e = {"value": round(max_over_ranks(a0.elapsed_time(a1) / args.steps), 3), "unit": "ms",
+        e2e = {"value": round(max(all_ranks(a0.elapsed_time(a1) / args.steps)), 3), "unit": "ms",
                "h2d_bytes_per_step": int(layout.slot_elements(rank) * 2), "d2h_bytes_per_step": 8,
                "api": "pytorch_opt_b200.dist.ShardedMuon.step_from_host (per-group H2D copies overlapped with "
                       "the grouped Muon kernels, C ABI) + NCCL all-gather"}
 
+    single = rank == 0 and world == 1
+    # ------------------------------------------------ GPU library bar (N = 1)
+    bar = None
+    if single and not args.no_library_bar:
+        mats = [layout.matrix(grads, i) for i in range(len(shapes))]
+        bar = gpu_library_bar(mats, dev)
     # --------------------------------------------------------- CPU baseline
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        t, kind, threads, desc = cpu_reference_sample()
-        cpu = {"value": round(t * total_flops / ns_flops(4096, 4096) * 1e3, 1), "unit": "ms", "cores": threads,
-               "kind": kind, "sample": desc}
+    if single and not args.no_cpu_baseline:
+        total, per, kind, threads, desc = cpu_reference_per_shape()
+        cpu = {"value": round(total, 1), "unit": "ms", "cores": threads, "kind": kind, "sample": desc,
+               "per_shape_ms": {f"{r}x{c}": round(per[(r, c)], 1) for r, c in LLAMA_DISTINCT}}
+    # ---------------------------------------- configs 1-4 on this GPU (N = 1)
+    secondary = None
+    if single and not args.no_secondary:
+        del sm, params, grads
+        torch.cuda.empty_cache()
+        secondary = run_secondary_all(dev, args, with_cpu=not args.no_cpu_baseline)
 
-    gemm_tflops = max_over_ranks(-gemm_tflops_local)  # slowest rank's rate
-    gemm_tflops = -gemm_tflops
     pk = peaks()
-    mix_peak = 1.0 / (0.6 / pk["bf16_sustained"] + 0.4 / (pk["bf16_sustained"] / 2))
     if rank == 0:
+        traffic, prof_fp, prof_match = profiled_traffic("launches_llama8b_muon_step.md")
         line = {
             "metric": METRIC, "value": round(step_ms, 3), "unit": "ms", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(step_ms, 3), "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "precision": "bf16 tensor-core products on NS steps 1-3, tf32 on steps 4-5, fp32 accumulation",
+            "precision": "bf16 tensor-core products on every NS step with the exact fp32 diagonal split of A and B "
+                         "in the epilogues; fp32 accumulation",
             "config": {"workload": "Muon step over Llama-3-8B matrix params (224 bf16 matrices, 5 NS steps)",
                        "ns_steps": 5, "momentum": 0.95, "nesterov": True,
                        "parallelism": f"per-matrix FLOP-balanced shard x{world} + NCCL all-gather"
@@ -299,20 +422,34 @@ def run_ours(args, rank, world, local_rank):
                          "kernel": "tc_gemm_pair_kernel (Newton-Schulz products, 256x256 tiles on SM pairs)",
                          "achieved": round(gemm_tflops, 1), "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
                          "frac": round(gemm_tflops / pk["bf16_sustained"], 3),
-                         "traffic": LLAMA_STEP_TRAFFIC if world == 1 else None,
-                         "traffic_unit": "DRAM bytes per step of all Newton-Schulz product launches (ncu "
-                                         "dram__bytes_read.sum + dram__bytes_write.sum; 1 GPU only, "
-                                         "profiles/launches_llama8b_muon_step.md)",
+                         "traffic": traffic if world == 1 else None,
+                         "traffic_unit": "DRAM bytes per 1-GPU step summed over the Newton-Schulz product launches "
+                                         "(ncu dram__bytes_read.sum + dram__bytes_write.sum, committed launch-list "
+                                         "summary)",
+                         "traffic_profiled_build": prof_fp, "traffic_matches_this_build": prof_match,
                          "peak_source": pk["source"] + " bf16 sustained (MEASURED_PEAKS.json)",
-                         "peak_bf16_tf32_mix": round(mix_peak, 1),
-                         "frac_of_mix": round(gemm_tflops / mix_peak, 3),
                          "how": "dense NS FLOPs of the rank's matrices / CUDA-event time of its Newton-Schulz "
-                                "calls inside the timed steps (includes two small packing kernels per call)"},
+                                "calls inside the timed steps (includes the norm and packing kernels); slowest rank"},
             "clocks": clk,
             "gpu_launches": int(launches),
             "e2e": e2e,
             "cpu_baseline": cpu,
         }
+        if bar is not None:
+            line["gpu_library_bar"] = bar
+        if world > 1:
+            fl = [layout.flops(r) / 1e12 for r in range(world)]
+            line["scaling_detail"] = {
+                "rank_step_ms": [round(x, 2) for x in step_ranks],
+                "rank_ns_compute_ms": [round(x, 2) for x in ns_ranks],
+                "rank_exposed_exchange_ms": [round(x, 2) for x in tail_ranks],
+                "rank_tflop": [round(x, 2) for x in fl],
+                "lpt_imbalance_max_over_mean": round(max(fl) / (sum(fl) / len(fl)), 4),
+                "exchange_chunks": layout.chunks,
+                "how": "per rank: CUDA-event time of its Newton-Schulz calls, and of the wait for the all-gathers "
+                       "still in flight after its last kernel (the exposed exchange)"}
+        if secondary is not None:
+            line["secondary"] = secondary
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -342,16 +479,17 @@ def _timed(fn, steps, warmup, dev, flush=None):
     return sum(a.elapsed_time(b) for a, b in pairs) / steps, clk
 
 
-def _line(args, metric, value, unit, hib, workload, tflops, clk, launches, cpu, extra=None, traffic=None):
+def _line(args, metric, value, unit, hib, workload, tflops, clk, launches, cpu, extra=None, traffic=None,
+          peak=None, peak_name="bf16 sustained"):
     pk = peaks()
+    peak = pk["bf16_sustained"] if peak is None else peak
     line = {"metric": metric, "value": round(value, 4), "unit": unit, "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": None, "higher_is_better": hib, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": workload, "l2": "flushed between timed calls (256 MiB write)"},
             "roofline": {"bound": "tensor", "kernel": "tc_gemm_pair_kernel", "achieved": round(tflops, 1),
-                         "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
-                         "frac": round(tflops / pk["bf16_sustained"], 3), "traffic": traffic,
-                         "peak_source": pk["source"] + " bf16 sustained (MEASURED_PEAKS.json)",
+                         "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(tflops / peak, 3), "traffic": traffic,
+                         "peak_source": pk["source"] + f" {peak_name} (MEASURED_PEAKS.json)",
                          "how": "dense algorithmic FLOPs of the call / its CUDA-event time"},
             "clocks": clk, "gpu_launches": launches, "e2e": None, "cpu_baseline": cpu}
     if extra:
@@ -368,45 +506,229 @@ def _cpu_time(fn, reps=1):
     return (time.perf_counter() - t0) / reps
 
 
+def _ref_module():
+    try:
+        from oracle import ref_native
+        return ref_native.load()
+    except Exception:
+        return None
+
+
+def cfg_ns768(dev, flush, steps, warmup, with_cpu):
+    """Config 1: NS5 of one 768 x 3072 fp32 N(0,1) matrix (seed 0)."""
+    from pytorch_opt_b200 import native
+    g = torch.Generator().manual_seed(0)
+    Gc = torch.randn(768, 3072, generator=g)
+    G = Gc.to(dev)
+    ms, clk = _timed(lambda: native.newton_schulz_orthogonalize(G, 5, 3.4445, -4.7750, 2.0315, 1e-7), steps, warmup,
+                     dev, flush)
+    fl = ns_flops(768, 3072)
+    cpu = None
+    ref = _ref_module()
+    if with_cpu and ref is not None:
+        t = _cpu_time(lambda: ref.newton_schulz_orthogonalize(Gc, 5, 3.4445, -4.7750, 2.0315, 1e-7), reps=3)
+        cpu = {"value": round(t * 1e3, 2), "unit": "ms", "cores": len(os.sched_getaffinity(0)), "kind": "reference",
+               "sample": "the reference's ATen NS5 (pytorch_opt_ops.cpp:65-81) on the same matrix, mean of 3"}
+    return {"metric": "NS5 768x3072 ms", "value": ms, "unit": "ms", "higher_is_better": False,
+            "workload": "NS5 of one 768x3072 fp32 matrix, N(0,1), seed 0 (config 1)", "tflops": fl / (ms * 1e-3) / 1e12,
+            "clocks": clk, "gpu_launches": 2 + 3 * 5, "cpu_baseline": cpu}
+
+
+def cfg_gpt2(dev, flush, steps, warmup, with_cpu):
+    """Config 2: Muon step over the 48 GPT-2-small matrices."""
+    from pytorch_opt_b200.muon import GroupedMuon, MuonGroup
+    shapes = [(768, 2304), (768, 768), (768, 3072), (3072, 768)]
+    groups, k = [], 0
+    for shp in shapes:
+        p = torch.empty(12, *shp, dtype=torch.bfloat16, device=dev)
+        gr = torch.empty_like(p)
+        for j in range(12):
+            fill_normal(p[j], 2000 + k, 0.02)
+            fill_normal(gr[j], 1000 + k, 0.02)
+            k += 1
+        groups.append(MuonGroup(p, gr))
+    opt = GroupedMuon(groups, lr=0.02, momentum=0.95, nesterov=True, ns_steps=5)
+    fl = 12 * sum(ns_flops(*s) for s in shapes)
+    ms, clk = _timed(opt.step, steps, warmup, dev, flush)
+    cpu = None
+    if with_cpu:
+        fn, kind, impl = _ref_ns_fn()
+        torch.set_num_threads(len(os.sched_getaffinity(0)))
+        per = {}
+        for i, shp in enumerate(shapes):
+            G = _llama_sample(shp, 1000 + i)
+            fn(G)
+            t0 = time.perf_counter()
+            fn(G)
+            per[shp] = (time.perf_counter() - t0) * 1e3
+        cpu = {"value": round(12 * sum(per.values()), 1), "unit": "ms", "cores": len(os.sched_getaffinity(0)),
+               "kind": kind, "sample": f"one NS5 per distinct shape by {impl}, x12 layers (the elementwise parts "
+                                       "of the reference's step are not timed)"}
+    return {"metric": "GPT-2-small Muon step ms", "value": ms, "unit": "ms", "higher_is_better": False,
+            "workload": "Muon step over 48 GPT-2-small matrices (bf16, 0.02 N(0,1), momentum 0.95 Nesterov, "
+                        "5 NS steps) (config 2)", "tflops": fl / (ms * 1e-3) / 1e12, "clocks": clk,
+            "gpu_launches": opt.launches_per_step(), "cpu_baseline": cpu}
+
+
+def cfg_shampoo(dev, flush, steps, warmup, with_cpu):
+    """Config 3: inverse 4th roots of 8 SPD factors per size d in {1024, 2048, 4096}."""
+    from pytorch_opt_b200 import _lib
+    lib = _lib.load()
+    res, clk = {}, None
+    for d in (1024, 2048, 4096):
+        g = torch.Generator(device=dev).manual_seed(d * 100)
+        Gs = torch.randn(8, d, 2 * d, generator=g, device=dev)
+        L = Gs @ Gs.mT / (2 * d) + 1e-6 * torch.eye(d, device=dev)
+        del Gs
+        out = torch.empty_like(L)
+        its = torch.zeros(8, dtype=torch.int32, device=dev)
+        nbytes = lib.po_root_workspace_bytes(8, d, 4)
+        ws = _lib.workspace(nbytes, dev)
+
+        def call():
+            _lib.check(lib.po_inverse_root(L.data_ptr(), 0, 8, d, d, d * d, out.data_ptr(), d, d * d, 4, 1e-8,
+                                           100, 1e-10, its.data_ptr(), ws.data_ptr(), nbytes,
+                                           _lib.stream_ptr(dev)), "root")
+        ms, c = _timed(call, steps, warmup, dev, flush)
+        n_it = its.tolist()
+        fl = sum(8.0 * d ** 3 * i for i in n_it)
+        res[d] = {"ms": round(ms, 3), "iters": n_it, "tflops": round(fl / (ms * 1e-3) / 1e12, 1)}
+        clk = c if d == 4096 else clk
+        del L, out, ws
+    cpu = None
+    ref = _ref_module()
+    if with_cpu and ref is not None:
+        torch.set_num_threads(len(os.sched_getaffinity(0)))
+        t = {}
+        for d in (1024, 2048):
+            g = torch.Generator().manual_seed(d * 100)
+            Gm = torch.randn(d, 2 * d, generator=g)
+            Lc = Gm @ Gm.T / (2 * d) + 1e-6 * torch.eye(d)
+            t0 = time.perf_counter()
+            ref.inverse_matrix_root(Lc, 4, 1e-8, "newton", True, 100, 1e-10)
+            t[d] = time.perf_counter() - t0
+        total = 8 * (t[1024] + t[2048] + 8 * t[2048])
+        cpu = {"value": round(total * 1e3, 1), "unit": "ms", "cores": len(os.sched_getaffinity(0)),
+               "kind": "reference", "per_factor_ms": {"1024": round(t[1024] * 1e3, 1), "2048": round(t[2048] * 1e3, 1)},
+               "sample": "the reference's ATen coupled Newton (fp64, pytorch_opt_ops.cpp:15-63) on one d=1024 and "
+                         "one d=2048 factor; total = 8 x (t1024 + t2048 + 8 t2048), d=4096 scaled from d=2048 by d^3"}
+    ms_all = sum(r["ms"] for r in res.values())
+    return {"metric": "Shampoo inverse 4th root TFLOP/s (8 x d=4096)", "value": res[4096]["tflops"],
+            "unit": "TFLOP/s", "higher_is_better": True,
+            "workload": "coupled-Newton inverse 4th roots of 8 SPD factors per size, L = G G^T/2d + 1e-6 I, "
+                        "damping 1e-8 (config 3)", "tflops": res[4096]["tflops"], "ms_all_sizes": round(ms_all, 3),
+            "per_size": res, "clocks": clk, "gpu_launches": None, "cpu_baseline": cpu,
+            "peak_split_bf16": peaks()["bf16_sustained"] / 3.0}
+
+
+def cfg_kfac(dev, flush, steps, warmup, with_cpu):
+    """Config 4: KFAC SYRK+EMA of A and G (8192 x 4096 bf16), then the pi-damped inverses."""
+    from pytorch_opt_b200 import native
+    g1 = torch.Generator(device=dev).manual_seed(1)
+    g2 = torch.Generator(device=dev).manual_seed(2)
+    a = torch.randn(8192, 4096, generator=g1, device=dev).bfloat16()
+    gr = torch.randn(8192, 4096, generator=g2, device=dev).bfloat16()
+    A = torch.empty(4096, 4096, device=dev)
+    Gf = torch.empty(4096, 4096, device=dev)
+    n = 8192
+    native.kron_syrk_ema_(A, a, 1.0 / n, 0.95, True)
+    native.kron_syrk_ema_(Gf, gr, float(n), 0.95, True)
+
+    def update():
+        native.kron_syrk_ema_(A, a, 1.0 / n, 0.95, False)
+        native.kron_syrk_ema_(Gf, gr, float(n), 0.95, False)
+    ms_u, clk = _timed(update, steps, warmup, dev, flush)
+    tr_a = float(A.diagonal().sum()) / 4096
+    tr_g = float(Gf.diagonal().sum()) / 4096
+    pi = math.sqrt(tr_a / tr_g)
+    ga, gg = pi * math.sqrt(1e-3), math.sqrt(1e-3) / pi
+
+    def inverse():
+        native.damped_inverse(A, ga)
+        native.damped_inverse(Gf, gg)
+    ms_i, _ = _timed(inverse, max(1, steps // 2), 1, dev, flush)
+    fl_u = 2 * 2.0 * 8192 * 4096 ** 2
+    cpu = None
+    if with_cpu:
+        torch.set_num_threads(len(os.sched_getaffinity(0)))
+        ac = torch.randn(8192, 4096, generator=torch.Generator().manual_seed(1)).bfloat16().float()
+        t_u = _cpu_time(lambda: ac.T @ ac / 8192)
+        Fc = ac[:2048, :1024].T @ ac[:2048, :1024] / 2048
+        t_e = _cpu_time(lambda: torch.linalg.eigh(Fc.double()))
+        cpu = {"value": round(2 * t_u * 1e3, 1), "unit": "ms", "cores": len(os.sched_getaffinity(0)),
+               "kind": "reference",
+               "inverse_ms_both_estimate": round(2 * 64 * t_e * 1e3, 1),
+               "sample": "the reference's factor product (torch fp32 a^T a / n on the CPU, kron.py:105-113) on the "
+                         "full 8192 x 4096 batch, x2 factors; its fp64 eigh inverse (kfac.py:134-138) timed at "
+                         "d = 1024 and scaled by d^3 to 4096 for both factors"}
+    return {"metric": "KFAC factor update ms (A and G, 8192x4096 -> 4096^2)", "value": ms_u, "unit": "ms",
+            "higher_is_better": False,
+            "workload": "KFAC SYRK+EMA of A = a^T a/n and G = (n g)^T (n g)/n, a, g 8192x4096 bf16, beta 0.95; "
+                        "then pi-damped inverses (lambda 1e-3) by coupled Newton p=1 (config 4)",
+            "tflops": fl_u / (ms_u * 1e-3) / 1e12, "damped_inverse_ms_both": round(ms_i, 3), "clocks": clk,
+            "gpu_launches": None, "cpu_baseline": cpu}
+
+
+SECONDARY = {"ns768": cfg_ns768, "gpt2": cfg_gpt2, "shampoo": cfg_shampoo, "kfac": cfg_kfac}
+
+
+def run_secondary_all(dev, args, with_cpu: bool) -> dict:
+    """Configs 1-4 on this GPU, each with its own clocks and CPU baseline (for the default line)."""
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    pk = peaks()
+    out = {}
+    for cfg, (name, steps, warmup) in enumerate((("ns768", 10, 3), ("gpt2", 5, 3), ("shampoo", 3, 1),
+                                                 ("kfac", 5, 3)), start=1):
+        r = SECONDARY[name](dev, flush, steps, warmup, with_cpu)
+        peak = r.pop("peak_split_bf16", pk["bf16_sustained"])
+        r["value"] = round(r["value"], 4)
+        r["tflops"] = round(r["tflops"], 1)
+        r["frac_of_peak"] = round(r["tflops"] / peak, 3)
+        r["peak"] = round(peak, 1)
+        r["peak_source"] = pk["source"] + (" bf16 sustained / 3 (split-bf16 products)" if name == "shampoo"
+                                           else " bf16 sustained")
+        r["steps"], r["warmup"] = steps, warmup
+        out[f"config{cfg}_{name}"] = r
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_secondary(args, rank):
     if rank != 0:
         return 0
-    from pytorch_opt_b200 import native
-    from pytorch_opt_b200.muon import GroupedMuon, MuonGroup
-
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    try:
-        from oracle import ref_native
-        ref = ref_native.load()
-    except Exception:
-        ref = None
     threads = len(os.sched_getaffinity(0))
     w = args.workload
-    if w in ("ns768", "ns4096"):
-        if w == "ns768":   # config 1
-            g = torch.Generator().manual_seed(0)
-            Gc = torch.randn(768, 3072, generator=g)
-            desc, fl = "NS5 of one 768x3072 fp32 matrix, N(0,1), seed 0 (config 1)", ns_flops(768, 3072)
-        else:              # a batch of q/o-shaped matrices: the profiling case of the main workload's products
-            g = torch.Generator().manual_seed(1000)
-            Gc = (torch.randn(4, 4096, 4096, generator=g) * 0.02).bfloat16()
-            desc, fl = "NS5 of 4 x 4096x4096 bf16 matrices (Llama q/o shape), 0.02 N(0,1)", 4 * ns_flops(4096, 4096)
+    if w in SECONDARY:
+        r = SECONDARY[w](dev, flush, args.steps, args.warmup, not args.no_cpu_baseline)
+        peak = r.pop("peak_split_bf16", None)
+        extra = {k: v for k, v in r.items() if k not in ("metric", "value", "unit", "higher_is_better", "workload",
+                                                         "tflops", "clocks", "gpu_launches", "cpu_baseline")}
+        launches = r["gpu_launches"] * args.steps if r["gpu_launches"] else None
+        _line(args, r["metric"], r["value"], r["unit"], r["higher_is_better"], r["workload"], r["tflops"],
+              r["clocks"], launches, r["cpu_baseline"], extra, peak=peak,
+              peak_name="bf16 sustained / 3 (split-bf16 products)" if peak else "bf16 sustained")
+        return 0
+    ref = _ref_module()
+    from pytorch_opt_b200 import native
+    if w == "ns4096":      # a batch of q/o-shaped matrices: the profiling case of the main workload's products
+        g = torch.Generator().manual_seed(1000)
+        Gc = (torch.randn(4, 4096, 4096, generator=g) * 0.02).bfloat16()
+        desc, fl = "NS5 of 4 x 4096x4096 bf16 matrices (Llama q/o shape), 0.02 N(0,1)", 4 * ns_flops(4096, 4096)
         G = Gc.to(dev)
         ms, clk = _timed(lambda: native.newton_schulz_orthogonalize(G, 5, 3.4445, -4.7750, 2.0315, 1e-7),
                          args.steps, args.warmup, dev, flush)
         cpu = None
         if ref is not None and not args.no_cpu_baseline:
-            one = Gc if Gc.dim() == 2 else Gc[0]
-            t = _cpu_time(lambda: ref.newton_schulz_orthogonalize(one, 5, 3.4445, -4.7750, 2.0315, 1e-7))
-            cpu = {"value": round(t * 1e3 * (fl / ns_flops(*one.shape)), 2), "unit": "ms", "cores": threads,
-                   "kind": "reference", "sample": "the reference's ATen NS5 on one matrix of the workload"}
-        m = min(G.shape[-2:])
-        launches = 2 + 3 * 5
-        _line(args, f"{'NS5 768x3072' if w == 'ns768' else 'NS5 4x4096^2'} ms", ms, "ms", False, desc,
-              fl / (ms * 1e-3) / 1e12, clk, launches * args.steps, cpu, {"ms_per_step": round(ms, 4)},
-              traffic=NS4096_CALL_TRAFFIC if w == "ns4096" else None)
+            t = _cpu_time(lambda: ref.newton_schulz_orthogonalize(Gc[0], 5, 3.4445, -4.7750, 2.0315, 1e-7))
+            cpu = {"value": round(t * 1e3 * 4, 2), "unit": "ms", "cores": threads, "kind": "reference",
+                   "sample": "the reference's ATen NS5 on one 4096^2 matrix of the workload, x4"}
+        traffic, prof_fp, prof_match = profiled_traffic("tc_gemm_pair_ns4096.md")
+        _line(args, "NS5 4x4096^2 ms", ms, "ms", False, desc, fl / (ms * 1e-3) / 1e12, clk, (2 + 3 * 5) * args.steps,
+              cpu, {"ms_per_step": round(ms, 4), "traffic_profiled_build": prof_fp,
+                    "traffic_matches_this_build": prof_match}, traffic=traffic)
         return 0
     if w == "gemm":        # the product kernel alone, beside cuBLAS on the same shape
         import ctypes
@@ -438,106 +760,6 @@ def run_secondary(args, rank):
               {"ms_per_step": round(ms, 4),
                "library_comparison": {"torch.matmul (cuBLAS) TFLOP/s": round(fl / (ms_lib * 1e-3) / 1e12, 1),
                                       "note": "cuBLAS writes a bf16/fp32 C of the operand type"}})
-        return 0
-    if w == "gpt2":        # config 2
-        shapes = [(768, 2304), (768, 768), (768, 3072), (3072, 768)]
-        groups, k = [], 0
-        for shp in shapes:
-            p = torch.empty(12, *shp, dtype=torch.bfloat16, device=dev)
-            gr = torch.empty_like(p)
-            for j in range(12):
-                fill_normal(p[j], 2000 + k, 0.02)
-                fill_normal(gr[j], 1000 + k, 0.02)
-                k += 1
-            groups.append(MuonGroup(p, gr))
-        opt = GroupedMuon(groups, lr=0.02, momentum=0.95, nesterov=True, ns_steps=5)
-        fl = 12 * sum(ns_flops(*s) for s in shapes)
-        ms, clk = _timed(opt.step, args.steps, args.warmup, dev, flush)
-        cpu = None
-        if ref is not None and not args.no_cpu_baseline:
-            gs = (torch.randn(768, 2304) * 0.02).bfloat16()
-            t = _cpu_time(lambda: ref.newton_schulz_orthogonalize(gs, 5, 3.4445, -4.7750, 2.0315, 1e-7))
-            cpu = {"value": round(t * 1e3 * fl / ns_flops(768, 2304), 1), "unit": "ms", "cores": threads,
-                   "kind": "reference", "sample": "the reference's ATen NS5 on one 768x2304 matrix, scaled by FLOPs"}
-        _line(args, "GPT-2-small Muon step ms", ms, "ms", False,
-              "Muon step over 48 GPT-2-small matrices (bf16, 0.02 N(0,1), momentum 0.95 Nesterov, 5 NS steps)",
-              fl / (ms * 1e-3) / 1e12, clk, opt.launches_per_step() * args.steps, cpu,
-              {"ms_per_step": round(ms, 4)})
-        return 0
-    if w == "shampoo":     # config 3
-        res = {}
-        lib_iters = {}
-        for d in (1024, 2048, 4096):
-            g = torch.Generator(device=dev).manual_seed(d * 100)
-            Gs = torch.randn(8, d, 2 * d, generator=g, device=dev)
-            L = Gs @ Gs.mT / (2 * d) + 1e-6 * torch.eye(d, device=dev)
-            del Gs
-            from pytorch_opt_b200 import _lib
-            lib = _lib.load()
-            out = torch.empty_like(L)
-            its = torch.zeros(8, dtype=torch.int32, device=dev)
-            nbytes = lib.po_root_workspace_bytes(8, d, 4)
-            ws = _lib.workspace(nbytes, dev)
-
-            def call():
-                _lib.check(lib.po_inverse_root(L.data_ptr(), 0, 8, d, d, d * d, out.data_ptr(), d, d * d, 4, 1e-8,
-                                               100, 1e-10, its.data_ptr(), ws.data_ptr(), nbytes,
-                                               _lib.stream_ptr(dev)), "root")
-            ms, clk = _timed(call, args.steps, args.warmup, dev, flush)
-            n_it = its.tolist()
-            fl = sum(8.0 * d ** 3 * i for i in n_it)
-            res[d] = {"ms": round(ms, 3), "iters": n_it[0], "tflops": round(fl / (ms * 1e-3) / 1e12, 1)}
-            lib_iters[d] = n_it
-            del L, out, ws
-        cpu = None
-        if ref is not None and not args.no_cpu_baseline:
-            g = torch.Generator().manual_seed(1024 * 100)
-            Gm = torch.randn(1024, 2048, generator=g)
-            Lc = Gm @ Gm.T / 2048 + 1e-6 * torch.eye(1024)
-            t = _cpu_time(lambda: ref.inverse_matrix_root(Lc, 4, 1e-8, "newton", True, 100, 1e-10))
-            cpu = {"value": round(t * 1e3 * 8 * 64, 1), "unit": "ms", "cores": threads, "kind": "reference",
-                   "sample": "the reference's ATen coupled Newton (fp64) on one d=1024 factor, x8 factors x (4096/1024)^3"}
-        _line(args, "Shampoo inverse 4th root TFLOP/s (8 x d=4096)", res[4096]["tflops"], "TFLOP/s", True,
-              "coupled-Newton inverse 4th roots of 8 SPD factors per size, L = G G^T/2d + 1e-6 I, damping 1e-8",
-              res[4096]["tflops"], clk, None, cpu, {"ms_per_step": res[4096]["ms"], "per_size": res})
-        return 0
-    if w == "kfac":        # config 4
-        g1 = torch.Generator(device=dev).manual_seed(1)
-        g2 = torch.Generator(device=dev).manual_seed(2)
-        a = torch.randn(8192, 4096, generator=g1, device=dev).bfloat16()
-        gr = torch.randn(8192, 4096, generator=g2, device=dev).bfloat16()
-        A = torch.empty(4096, 4096, device=dev)
-        Gf = torch.empty(4096, 4096, device=dev)
-        n = 8192
-        native.kron_syrk_ema_(A, a, 1.0 / n, 0.95, True)
-        native.kron_syrk_ema_(Gf, gr, float(n), 0.95, True)
-
-        def update():
-            native.kron_syrk_ema_(A, a, 1.0 / n, 0.95, False)
-            native.kron_syrk_ema_(Gf, gr, float(n), 0.95, False)
-        ms_u, clk = _timed(update, args.steps, args.warmup, dev, flush)
-        tr_a = float(A.diagonal().sum()) / 4096
-        tr_g = float(Gf.diagonal().sum()) / 4096
-        pi = math.sqrt(tr_a / tr_g)
-        ga, gg = pi * math.sqrt(1e-3), math.sqrt(1e-3) / pi
-
-        def inverse():
-            native.damped_inverse(A, ga)
-            native.damped_inverse(Gf, gg)
-        ms_i, _ = _timed(inverse, max(1, args.steps // 2), 1, dev, flush)
-        fl_u = 2 * 2.0 * 8192 * 4096 ** 2
-        cpu = None
-        if not args.no_cpu_baseline:
-            ac = torch.randn(2048, 4096).float()
-            t = _cpu_time(lambda: ac.T @ ac)
-            cpu = {"value": round(t * 1e3 * 4 * 2, 1), "unit": "ms", "cores": threads, "kind": "reference",
-                   "sample": "the reference's factor GEMM (torch fp32 a^T a, kron.py:113) on 2048 of the 8192 rows, "
-                             "x4 rows x2 factors (update only; its fp64 eigh inverse is ~77 s per factor on 8 cores)"}
-        _line(args, "KFAC factor update ms (A and G, 8192x4096 -> 4096^2)", ms_u, "ms", False,
-              "KFAC SYRK+EMA of A = a^T a/n and G = (n g)^T (n g)/n, a, g 8192x4096 bf16, beta 0.95; "
-              "then pi-damped inverses (lambda 1e-3) by coupled Newton p=1",
-              fl_u / (ms_u * 1e-3) / 1e12, clk, None, cpu,
-              {"ms_per_step": round(ms_u, 4), "damped_inverse_ms_both": round(ms_i, 3)})
         return 0
     if w == "ekfac":       # section 8f rank 4: EKFAC rotated-diagonal precondition of one layer
         m = n = 4096
@@ -638,6 +860,10 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-library-bar", action="store_true",
+                    help="skip the torch/cuBLAS Newton-Schulz bar of the default workload")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip configs 1-4 in the default workload's line")
     ap.add_argument("--workload", default="llama8b",
                     choices=("llama8b", "ns768", "ns4096", "gpt2", "shampoo", "kfac", "gemm", "ekfac", "kfac_split"),
                     help="llama8b (default, config 5); the others are single-GPU measurements of configs 1-4, "
