@@ -458,25 +458,39 @@ def run_ours(args, rank, world, local_rank):
 
 
 # ------------------------------------------------- secondary workloads (1 GPU)
-def _timed(fn, steps, warmup, dev, flush=None):
-    """Per-call CUDA-event time (ms), L2 flushed between calls (outside the timed intervals)."""
+MIN_TIMED_SECONDS = 1.0
+
+
+def _timed(fn, steps, warmup, dev, flush=None, min_seconds=None):
+    """Per-call CUDA-event time (ms), L2 flushed between calls (outside the timed intervals).
+
+    Short calls are repeated in rounds of ``steps`` until the timed region
+    lasts at least ``min_seconds``, so that the clock sampler (200 ms period)
+    sees it; the time is the mean over every timed call."""
+    if min_seconds is None:
+        min_seconds = MIN_TIMED_SECONDS
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize(dev)
     clocks = ClockSampler(dev)
     clocks.start()
     pairs = []
-    for _ in range(steps):
-        if flush is not None:
-            flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        fn()
-        b.record()
-        pairs.append((a, b))
-    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    while True:
+        for _ in range(steps):
+            if flush is not None:
+                flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            pairs.append((a, b))
+        torch.cuda.synchronize(dev)
+        if time.perf_counter() - t0 >= min_seconds or len(pairs) >= 200 * steps:
+            break
     clk = clocks.stop()
-    return sum(a.elapsed_time(b) for a, b in pairs) / steps, clk
+    clk["timed_calls"] = len(pairs)
+    return sum(a.elapsed_time(b) for a, b in pairs) / len(pairs), clk
 
 
 def _line(args, metric, value, unit, hib, workload, tflops, clk, launches, cpu, extra=None, traffic=None,
@@ -864,6 +878,9 @@ def main(argv=None) -> int:
                     help="skip the torch/cuBLAS Newton-Schulz bar of the default workload")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip configs 1-4 in the default workload's line")
+    ap.add_argument("--min-timed-seconds", type=float, default=1.0,
+                    help="single-GPU workloads repeat their timed calls until the timed region lasts this long "
+                         "(so the clock sampler sees it); 0 times exactly --steps calls (for profiling)")
     ap.add_argument("--workload", default="llama8b",
                     choices=("llama8b", "ns768", "ns4096", "gpt2", "shampoo", "kfac", "gemm", "ekfac", "kfac_split"),
                     help="llama8b (default, config 5); the others are single-GPU measurements of configs 1-4, "
@@ -874,6 +891,8 @@ def main(argv=None) -> int:
     ap.add_argument("--exchange-chunks", type=int, default=None,
                     help="all-gather chunks per step for N > 1 (default 4; 1 = one all-gather after the local step)")
     args = ap.parse_args(argv)
+    global MIN_TIMED_SECONDS
+    MIN_TIMED_SECONDS = args.min_timed_seconds
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -49,6 +49,14 @@ int po_device_error(int reset);
 /* Library version string. */
 const char* po_version(void);
 
+/* Self-test of the kernels' bounded waits (no counterpart in the reference):
+ * launches one block that waits on an mbarrier nothing arms, with the wait
+ * functions the product kernels use (sleeping = 1: the epilogue's sleeping
+ * wait) and a limit of limit_ns instead of their 5 s. The kernel gives up,
+ * records code 5 in the device error word and returns; po_device_error()
+ * then reports 5 and the context stays usable. */
+int po_selftest_wait_timeout(unsigned long long limit_ns, int sleeping, void* stream);
+
 /* ------------------------------------------------------------------------
  * Newton–Schulz orthogonalisation.
  * Replaces pytorch_opt/ops/csrc/pytorch_opt_ops.cpp:65-81
@@ -198,6 +206,27 @@ int po_muon_momentum(const void* g, void* buf, void* u, int dtype, long long n, 
                      void* stream);
 int po_muon_apply(void* p, const void* o, int dtype, long long n, float lr_eff, float decay, double* sq_sum,
                   void* stream);
+
+/* ------------------------------------------------------------------------
+ * One fused Muon step of a group of same-shape matrices: replaces, per
+ * matrix, pytorch_opt/optim/muon.py:79-93 (momentum :82, Nesterov :83,
+ * newton_schulz_orthogonalize :85, decoupled decay :87-88, update :91 and
+ * the update_rms sum :92). g, buf, p: [batch][rows][cols] contiguous of
+ * `dtype` (PO_BF16 / PO_F32); buf and p are updated in place:
+ *   buf <- buf*momentum + g;  u <- nesterov ? g + momentum*buf : buf
+ *   O = NS_steps(u) (as po_newton_schulz, default schedule, cast to dtype)
+ *   p <- p*decay (when decay != 1);  p <- p - lr_eff*O;  *sq_sum += sum(O^2)
+ * with the reference's roundings (every in-place op rounds to dtype; the
+ * add's alpha is rounded to dtype). The momentum pass also sums each
+ * matrix's ||u||_F^2, bf16 u is read directly by the first products (no
+ * packed copy), and the last product's epilogue updates p, so O is never
+ * stored. o_out (nullable, [batch][rows][cols] of dtype) also receives O.
+ * sq_sum: device fp64, nullable, accumulated (not reset).
+ * ---------------------------------------------------------------------- */
+size_t po_muon_step_workspace_bytes(long long batch, long long rows, long long cols, int dtype);
+int po_muon_step(const void* g, void* buf, void* p, int dtype, long long batch, long long rows, long long cols,
+                 float momentum, int nesterov, int ns_steps, float a, float b, float c, float eps, float lr_eff,
+                 float decay, double* sq_sum, void* o_out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
  * General batched product used by the ops above, exported for tests:

@@ -26,6 +26,7 @@ SIGNATURES = {
     "po_last_error": (ctypes.c_char_p, []),
     "po_device_error": (_i, [_i]),
     "po_version": (ctypes.c_char_p, []),
+    "po_selftest_wait_timeout": (_i, [ctypes.c_ulonglong, _i, _vp]),
     "po_ns_workspace_bytes": (_sz, [_ll, _ll, _ll]),
     "po_newton_schulz": (_i, [_vp, _i, _ll, _ll, _ll, _ll, _ll, _vp, _ll, _ll, _i, _f, _f, _f, _f, _i, _vp, _sz,
                               _vp]),
@@ -45,6 +46,9 @@ SIGNATURES = {
                                    _vp]),
     "po_muon_momentum": (_i, [_vp, _vp, _vp, _i, _ll, _f, _i, _vp]),
     "po_muon_apply": (_i, [_vp, _vp, _i, _ll, _f, _f, _vp, _vp]),
+    "po_muon_step_workspace_bytes": (_sz, [_ll, _ll, _ll, _i]),
+    "po_muon_step": (_i, [_vp, _vp, _vp, _i, _ll, _ll, _ll, _f, _i, _i, _f, _f, _f, _f, _f, _f, _vp, _vp, _vp, _sz,
+                          _vp]),
     "po_matmul_workspace_bytes": (_sz, [_ll, _ll, _ll, _ll, _i, _i]),
     "po_matmul": (_i, [_vp, _ll, _ll, _i, _vp, _ll, _ll, _i, _vp, _ll, _ll, _i, _i, _ll, _ll, _ll, _ll, _f, _f,
                        _vp, _sz, _vp]),

@@ -49,4 +49,10 @@ int launch_split_bf16(const AnyMat& src, int batch, __nv_bfloat16* hi, __nv_bflo
 int launch_split_tf32(const AnyMat& src, int batch, float* hi, float* lo, long long ld_dst, long long bs_dst,
                       cudaStream_t s);
 
+// Muon momentum (pytorch_opt/optim/muon.py:82-83) of a [batch][per] group of
+// dtype PO_BF16 / PO_F32: buf <- buf*mu + g, u <- nesterov ? g + mu*buf :
+// buf, and sums[b] += sum(u^2) of matrix b (sums must be zeroed).
+int launch_momentum_sumsq(const void* g, void* buf, void* u, int dtype, long long batch, long long per, float mu,
+                          int nesterov, double* sums, cudaStream_t s);
+
 }  // namespace po

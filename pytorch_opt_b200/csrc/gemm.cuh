@@ -105,6 +105,10 @@ struct Epilogue {
   // beta + in0_rowcoef[b][i] instead of beta (nullable).
   const float* in0_rowcoef;
   long long in0_rowcoef_bs;
+  // The same for the right operand's diagonal, U X with X on the left (X D):
+  // in[0]'s coefficient for column j is beta + in0_colcoef[b][j] (nullable).
+  const float* in0_colcoef;
+  long long in0_colcoef_bs;
   // Diagonal of the stored result: diag_out[b][i] = D_ii (nullable; written by
   // the thread holding the diagonal element, on diagonal tiles).
   float* diag_out;
@@ -112,6 +116,35 @@ struct Epilogue {
   // Per batch: += sum of the stored diagonal values D_ii (nullable): the
   // trace of the result, for KFAC's pi-split damping.
   double* red_trace;
+  // Symmetric diagonal split against the addend (nullable): in[0] is the
+  // fp32 master of a symmetric operand A whose diagonal was zeroed for the
+  // tensor cores (the product is F F, F = A off its diagonal) and dsym is
+  // that diagonal, contiguous [batch][M]. With one row read of A the
+  // epilogue forms alpha*acc + (beta0 + alpha*(d_i + d_j)) A_ij - [i==j]
+  // alpha d_i^2 = alpha*(A A) + beta0*A.
+  const float* dsym;
+  long long dsym_bs;
+  // Per-batch scales read on the device (nullable): alpha is multiplied by
+  // alpha_scale[b], in[0]'s coefficient (beta, plus in0_rowcoef) by in_scale[b].
+  const float* alpha_scale;
+  const float* in_scale;
+  // red_sumsq: 1 = every batch item adds into red_sumsq[0].
+  int red_sumsq_shared;
+  // Muon's parameter update from the product's values (nullable mu_p):
+  // o = v rounded to the parameter type, p <- round(round(p * mu_decay) +
+  // mu_alpha * o) (the decay only when mu_use_decay), and red_sumsq gets o^2.
+  // p is [batch][..] with pitch mu_ld, batch pitch mu_bs, laid out like the
+  // product. Outputs, if any, are still written.
+  void* mu_p;
+  long long mu_ld, mu_bs;
+  int mu_bf16;  // parameter type: 1 = bf16, 0 = fp32
+  int mu_vec;   // 16-byte vector access legal
+  int mu_use_decay;
+  float mu_decay, mu_alpha;
+  // Triangular products: on diagonal tiles store only j <= i and mirror the
+  // lower half to the upper (bit-symmetric results when the (i, j) and
+  // (j, i) accumulations differ, as for split passes hi*lo + lo*hi).
+  int sym_diag;
 };
 
 struct alignas(64) GemmParams {
@@ -256,11 +289,12 @@ __device__ __forceinline__ void add_col_typed(const T* p, long long ld, int nv, 
   }
 }
 
-__device__ __forceinline__ void add_col(const EpiIn& in, int b, int row, int col0, int ncols, float (&x)[EC]) {
+__device__ __forceinline__ void add_col(const EpiIn& in, float beta, int b, int row, int col0, int ncols,
+                                        float (&x)[EC]) {
   const long long off = static_cast<long long>(b) * in.bstride + row + static_cast<long long>(col0) * in.ld;
   const int nv = ncols - col0;
-  if (in.kind == IN_F32) add_col_typed(static_cast<const float*>(in.ptr) + off, in.ld, nv, in.beta, x);
-  else add_col_typed(static_cast<const __nv_bfloat16*>(in.ptr) + off, in.ld, nv, in.beta, x);
+  if (in.kind == IN_F32) add_col_typed(static_cast<const float*>(in.ptr) + off, in.ld, nv, beta, x);
+  else add_col_typed(static_cast<const __nv_bfloat16*>(in.ptr) + off, in.ld, nv, beta, x);
 }
 
 __device__ __forceinline__ void store_elem(const EpiOut& o, long long off, float v) {
@@ -383,6 +417,47 @@ __device__ __forceinline__ void load_row_f32(const EpiIn& in, int b, int row, in
   }
 }
 
+// Load EC consecutive elements of row `row` of an fp32 or bf16 input as fp32
+// (zeros past ncols).
+__device__ __forceinline__ void load_row_any(const EpiIn& in, int b, int row, int col0, int ncols, float (&x)[EC]) {
+  if (in.kind == IN_F32) {
+    load_row_f32(in, b, row, col0, ncols, x);
+    return;
+  }
+  const __nv_bfloat16* p = static_cast<const __nv_bfloat16*>(in.ptr) + static_cast<long long>(b) * in.bstride +
+                           static_cast<long long>(row) * in.ld + col0;
+  if (in.vec && col0 + EC <= ncols) {
+#pragma unroll
+    for (int q = 0; q < EC / 8; ++q) {
+      const uint4 u = reinterpret_cast<const uint4*>(p)[q];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        x[8 * q + 2 * e] = f.x;
+        x[8 * q + 2 * e + 1] = f.y;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < EC; ++j) x[j] = (col0 + j < ncols) ? __bfloat162float(p[j]) : 0.0f;
+  }
+}
+
+// EC consecutive fp32 values of a vector from index col0 (zeros past n).
+__device__ __forceinline__ void load_vec_f32(const float* d, int col0, int n, float (&x)[EC]) {
+  if (col0 + EC <= n && (reinterpret_cast<uintptr_t>(d + col0) & 15) == 0) {
+#pragma unroll
+    for (int q = 0; q < EC / 4; ++q) {
+      const float4 f = reinterpret_cast<const float4*>(d + col0)[q];
+      x[4 * q] = f.x; x[4 * q + 1] = f.y; x[4 * q + 2] = f.z; x[4 * q + 3] = f.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < EC; ++j) x[j] = (col0 + j < n) ? d[col0 + j] : 0.0f;
+  }
+}
+
 // Store to output `o`, honouring its zero-diagonal flag (jd: column of the
 // diagonal within this chunk, or out of range).
 __device__ __forceinline__ void store_out(const EpiOut& o, int b, int row, int col0, int ncols, int jd,
@@ -420,8 +495,11 @@ __device__ __forceinline__ void epilogue_prefetch(const GemmParams& P, int b, in
   ncols = min(ncols, P.N - col0);
 #pragma unroll
   for (int i = 0; i < kMaxEpiIn; ++i)
-    if (i < E.nin) prefetch_row_segment(E.in[i].ptr, E.in[i].kind == IN_F32 ? 4 : 2, E.in[i].ld, E.in[i].bstride, b, row,
-                                        col0, ncols);
+    if (i < E.nin)
+      prefetch_row_segment(E.in[i].ptr, E.in[i].kind == IN_F32 ? 4 : 2, E.in[i].ld, E.in[i].bstride, b, row, col0,
+                           ncols);
+  if (E.mu_p != nullptr)
+    prefetch_row_segment(E.mu_p, E.mu_bf16 ? 2 : 4, E.mu_ld, E.mu_bs, b, row, col0, ncols);
   if (E.diag_split) {
     prefetch_row_segment(E.dU.ptr, 4, E.dU.ld, E.dU.bstride, b, row, col0, ncols);
     prefetch_row_segment(E.dV.ptr, 4, E.dV.ld, E.dV.bstride, b, row, col0, ncols);
@@ -433,6 +511,75 @@ __device__ __forceinline__ void red_update(float& red, float d) {
   red = (d != d) ? __int_as_float(0x7f800000) : fmaxf(red, d);
 }
 
+// Muon's in-place parameter update from the chunk's values v (see
+// Epilogue::mu_p); red += sum of the rounded update squared. The roundings
+// follow the reference's in-place ops on the parameter dtype
+// (pytorch_opt/optim/muon.py:87-91): O is the Newton-Schulz result cast to
+// the parameter dtype, p.mul_(decay) rounds, p.add_(O, alpha) rounds once.
+__device__ __forceinline__ float mu_round(float x, int bf16) {
+  return bf16 ? __bfloat162float(__float2bfloat16_rn(x)) : x;
+}
+
+__device__ __forceinline__ void muon_apply_chunk(const Epilogue& E, int b, int row, int col0, int ncols,
+                                                 const float (&v)[EC], float& red) {
+  const long long base = static_cast<long long>(b) * E.mu_bs;
+  float o[EC];
+#pragma unroll
+  for (int j = 0; j < EC; ++j) {
+    o[j] = (col0 + j < ncols) ? mu_round(v[j], E.mu_bf16) : 0.0f;
+    red = fmaf(o[j], o[j], red);
+  }
+  if (E.mu_vec && col0 + EC <= ncols) {
+    if (E.mu_bf16) {
+      __nv_bfloat16* p = static_cast<__nv_bfloat16*>(E.mu_p) + base + static_cast<long long>(row) * E.mu_ld + col0;
+#pragma unroll
+      for (int q = 0; q < EC / 8; ++q) {
+        uint4 u = reinterpret_cast<const uint4*>(p)[q];
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float2 f = __bfloat1622float2(h[e]);
+          if (E.mu_use_decay) {
+            f.x = mu_round(f.x * E.mu_decay, 1);
+            f.y = mu_round(f.y * E.mu_decay, 1);
+          }
+          h[e] = __floats2bfloat162_rn(fmaf(E.mu_alpha, o[8 * q + 2 * e], f.x), fmaf(E.mu_alpha, o[8 * q + 2 * e + 1], f.y));
+        }
+        reinterpret_cast<uint4*>(p)[q] = u;
+      }
+    } else {
+      float* p = static_cast<float*>(E.mu_p) + base + static_cast<long long>(row) * E.mu_ld + col0;
+#pragma unroll
+      for (int q = 0; q < EC / 4; ++q) {
+        float4 f = reinterpret_cast<const float4*>(p)[q];
+        float* fx = reinterpret_cast<float*>(&f);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float pd = E.mu_use_decay ? fx[e] * E.mu_decay : fx[e];
+          fx[e] = fmaf(E.mu_alpha, o[4 * q + e], pd);
+        }
+        reinterpret_cast<float4*>(p)[q] = f;
+      }
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < EC; ++j) {
+    if (col0 + j >= ncols) continue;
+    const long long off = base + static_cast<long long>(row) * E.mu_ld + col0 + j;
+    if (E.mu_bf16) {
+      __nv_bfloat16* p = static_cast<__nv_bfloat16*>(E.mu_p) + off;
+      float f = __bfloat162float(*p);
+      if (E.mu_use_decay) f = mu_round(f * E.mu_decay, 1);
+      *p = __float2bfloat16_rn(fmaf(E.mu_alpha, o[j], f));
+    } else {
+      float* p = static_cast<float*>(E.mu_p) + off;
+      const float f = E.mu_use_decay ? *p * E.mu_decay : *p;
+      *p = fmaf(E.mu_alpha, o[j], f);
+    }
+  }
+}
+
 // Epilogue for one EC-column chunk held by one thread (one row).
 __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCoord& tc, int row, int col0,
                                                bool mirror, const float (&acc)[EC], float& red) {
@@ -441,7 +588,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCo
   if (row >= P.M) return;
   const int jd = row - col0;  // diagonal column within this chunk, if any
   float v[EC];
-  const bool same = E.diag_split || E.mirror_same;
+  const bool same = E.diag_split || E.mirror_same || E.dsym != nullptr;
   if (mirror && !same) {
     // Element (row, c) of an off-diagonal tile of a symmetric product is also
     // element (c, row): rebuild it with the addends read at (c, row) and
@@ -450,7 +597,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCo
     for (int j = 0; j < EC; ++j) v[j] = E.alpha * acc[j];
 #pragma unroll
     for (int i = 0; i < kMaxEpiIn; ++i)
-      if (i < E.nin) add_col(E.in[i], tc.b, row, col0, N, v);
+      if (i < E.nin) add_col(E.in[i], E.in[i].beta, tc.b, row, col0, N, v);
 #pragma unroll
     for (int o = 0; o < kMaxEpiOut; ++o)
       if (o < E.nout) store_col(E.out[o], tc.b, row, col0, N, v);
@@ -460,9 +607,25 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCo
         if (col0 + j < N) red_update(red, fabsf(v[j]));
     }
   }
+  const float alpha = E.alpha_scale != nullptr ? E.alpha * E.alpha_scale[tc.b] : E.alpha;
 #pragma unroll
-  for (int j = 0; j < EC; ++j) v[j] = E.alpha * acc[j];
-  if (E.diag_split) {
+  for (int j = 0; j < EC; ++j) v[j] = alpha * acc[j];
+  int first_in = 0;
+  if (E.dsym != nullptr) {
+    // alpha*(F F) + alpha*(D A + A D - D^2) + beta0*A from one row of A.
+    const float* d = E.dsym + static_cast<long long>(tc.b) * E.dsym_bs;
+    const float di = d[row];
+    float a_row[EC], dj[EC];
+    load_row_f32(E.in[0], tc.b, row, col0, N, a_row);
+    load_vec_f32(d, col0, N, dj);
+    const float beta0 = E.in[0].beta;
+#pragma unroll
+    for (int j = 0; j < EC; ++j) {
+      v[j] = fmaf(fmaf(alpha, di + dj[j], beta0), a_row[j], v[j]);
+      if (j == jd) v[j] -= alpha * di * di;
+    }
+    first_in = 1;
+  } else if (E.diag_split) {
     const float* U = static_cast<const float*>(E.dU.ptr) + static_cast<long long>(tc.b) * E.dU.bstride;
     const float* V = static_cast<const float*>(E.dV.ptr) + static_cast<long long>(tc.b) * E.dV.bstride;
     const float u = U[static_cast<long long>(row) * (E.dU.ld + 1)];
@@ -474,7 +637,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCo
       const float vj = (col0 + j < N) ? V[static_cast<long long>(col0 + j) * (E.dV.ld + 1)] : 0.0f;
       float t = fmaf(u, vr[j], ur[j] * vj);
       if (j == jd) t -= u * vj;
-      v[j] = fmaf(E.alpha, t, v[j]);
+      v[j] = fmaf(alpha, t, v[j]);
     }
   }
   if (E.gamma != 0.0f) {
@@ -484,9 +647,22 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCo
   }
 #pragma unroll
   for (int i = 0; i < kMaxEpiIn; ++i) {
-    if (i < E.nin) {
+    if (i < E.nin && i >= first_in) {
       float beta = E.in[i].beta;
-      if (i == 0 && E.in0_rowcoef != nullptr) beta += E.in0_rowcoef[static_cast<long long>(tc.b) * E.in0_rowcoef_bs + row];
+      if (i == 0) {
+        if (E.in0_rowcoef != nullptr) beta += E.in0_rowcoef[static_cast<long long>(tc.b) * E.in0_rowcoef_bs + row];
+        if (E.in0_colcoef != nullptr) {
+          // x_j += (beta + cc_j) * scale * C0(row, j)
+          const float sc = E.in_scale != nullptr ? E.in_scale[tc.b] : 1.0f;
+          float cc[EC], cv[EC];
+          load_vec_f32(E.in0_colcoef + static_cast<long long>(tc.b) * E.in0_colcoef_bs, col0, N, cc);
+          load_row_any(E.in[0], tc.b, row, col0, N, cv);
+#pragma unroll
+          for (int j = 0; j < EC; ++j) v[j] = fmaf((beta + cc[j]) * sc, cv[j], v[j]);
+          continue;
+        }
+        if (E.in_scale != nullptr) beta *= E.in_scale[tc.b];
+      }
       add_row(E.in[i], beta, tc.b, row, col0, N, v);
     }
   }
@@ -511,9 +687,34 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCo
       }
     }
   }
+  if (E.mu_p != nullptr) {
+    muon_apply_chunk(E, tc.b, row, col0, N, v, red);
 #pragma unroll
-  for (int o = 0; o < kMaxEpiOut; ++o)
-    if (o < E.nout) store_out(E.out[o], tc.b, row, col0, N, jd, v);
+    for (int o = 0; o < kMaxEpiOut; ++o)
+      if (o < E.nout) store_out(E.out[o], tc.b, row, col0, N, jd, v);
+    return;  // plain products only: no mirrored half
+  }
+  if (E.sym_diag && P.tri && !mirror) {
+    // Diagonal tile: keep the lower half, written to both (i, j) and (j, i).
+#pragma unroll
+    for (int o = 0; o < kMaxEpiOut; ++o) {
+      if (o >= E.nout) continue;
+      const EpiOut& eo = E.out[o];
+      const long long base = static_cast<long long>(tc.b) * eo.bstride;
+#pragma unroll
+      for (int j = 0; j < EC; ++j) {
+        const int c = col0 + j;
+        if (c >= N || c > row) continue;
+        const float w = (eo.zero_diag && c == row) ? 0.0f : v[j];
+        store_elem(eo, base + static_cast<long long>(row) * eo.ld + c, w);
+        if (c < row) store_elem(eo, base + static_cast<long long>(c) * eo.ld + row, w);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int o = 0; o < kMaxEpiOut; ++o)
+      if (o < E.nout) store_out(E.out[o], tc.b, row, col0, N, jd, v);
+  }
   if (E.red_absmax != nullptr) {
 #pragma unroll
     for (int j = 0; j < EC; ++j)
@@ -767,11 +968,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
           ++ucount;
         }
         if (!ok) break;
-#pragma unroll
+        // One inlined copy of the epilogue: the chunk's registers are picked
+        // by a switch over compile-time offsets (racc stays in registers).
+#pragma unroll 1
         for (int c = 0; c < HC; ++c) {
           float f[EC];
+          static_assert(!CHUNKED || HC == 4, "chunked epilogue: four chunks per column half");
+          switch (c) {
+            case 0: {
 #pragma unroll
-          for (int j = 0; j < EC; ++j) f[j] = racc[c * EC + j];
+              for (int j = 0; j < EC; ++j) f[j] = racc[j];
+              break;
+            }
+            case 1: {
+#pragma unroll
+              for (int j = 0; j < EC; ++j) f[j] = racc[EC + j];
+              break;
+            }
+            case 2: {
+#pragma unroll
+              for (int j = 0; j < EC; ++j) f[j] = racc[2 * EC + j];
+              break;
+            }
+            default: {
+#pragma unroll
+              for (int j = 0; j < EC; ++j) f[j] = racc[3 * EC + j];
+              break;
+            }
+          }
           epilogue_chunk(P, tc, row, tc.nt * BN + (c_lo + c) * EC, mirror, f, red);
         }
       } else {
@@ -803,7 +1027,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_kernel(const __grid_c
       } else if (P.epi.red_sumsq != nullptr) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) red += __shfl_xor_sync(0xffffffffu, red, o);
-        if (lane == 0) atomicAdd(P.epi.red_sumsq + tc.b, static_cast<double>(red));
+        if (lane == 0) atomicAdd(P.epi.red_sumsq + (P.epi.red_sumsq_shared ? 0 : tc.b), static_cast<double>(red));
       }
     }
   }

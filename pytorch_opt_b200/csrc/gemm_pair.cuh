@@ -330,7 +330,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
       } else if (P.epi.red_sumsq != nullptr) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) red += __shfl_xor_sync(0xffffffffu, red, o);
-        if (lane == 0) atomicAdd(P.epi.red_sumsq + tc.b, static_cast<double>(red));
+        if (lane == 0) atomicAdd(P.epi.red_sumsq + (P.epi.red_sumsq_shared ? 0 : tc.b), static_cast<double>(red));
       }
     }
   }

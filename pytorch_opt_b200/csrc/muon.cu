@@ -146,6 +146,58 @@ __global__ void apply_kernel(T* __restrict__ p, const T* __restrict__ o, long lo
   }
 }
 
+// Momentum of a [batch][per] group (blockIdx.y = matrix) with the squared
+// Frobenius norm of each matrix's u summed on the way: sums[b] += sum(u^2)
+// over the values as stored (rounded to T). This is the norm of the
+// Newton-Schulz pre-normalisation, so no separate pass over u is needed.
+template <typename T>
+__global__ void momentum_sumsq_kernel(const T* __restrict__ g, T* __restrict__ buf, T* __restrict__ u, long long per,
+                                      float mu, int nesterov, int vec, double* __restrict__ sums) {
+  const MomentumOp<T> op{mu, round_to<T>(mu), nesterov};
+  const long long off = static_cast<long long>(blockIdx.y) * per;
+  g += off;
+  buf += off;
+  u += off;
+  constexpr int N = Vec<T>::N;
+  const long long tid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  const long long nvec = vec ? per / N : 0;
+  double acc = 0.0;
+  for (long long v = tid; v < nvec; v += stride) {
+    float gf[N], bf[N], of[N];
+    Vec<T>::load(g + v * N, gf);
+    Vec<T>::load(buf + v * N, bf);
+    float part = 0.0f;
+#pragma unroll
+    for (int e = 0; e < N; ++e) {
+      op(gf[e], bf[e], of[e]);
+      const float r = round_to<T>(of[e]);
+      part = fmaf(r, r, part);
+    }
+    acc += part;
+    Vec<T>::store(buf + v * N, bf);
+    Vec<T>::store(u + v * N, of);
+  }
+  for (long long i = nvec * N + tid; i < per; i += stride) {
+    float b = ld(buf, i), o;
+    op(ld(g, i), b, o);
+    buf[i] = cvt<T>(b);
+    u[i] = cvt<T>(o);
+    const float r = round_to<T>(o);
+    acc += static_cast<double>(r) * r;
+  }
+  __shared__ double part[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += part[w];
+    atomicAdd(sums + blockIdx.y, t);
+  }
+}
+
 bool aligned16(const void* a, const void* b, const void* c = nullptr) {
   return ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(c)) & 15) == 0;
 }
@@ -157,6 +209,31 @@ int grid_for(long long n) {
 }
 
 }  // namespace
+
+int launch_momentum_sumsq(const void* g, void* buf, void* u, int dtype, long long batch, long long per, float mu,
+                          int nesterov, double* sums, cudaStream_t s) {
+  if (batch <= 0 || per <= 0) return PO_OK;
+  if (batch > 65535) return set_error(PO_ERR_ARG, "muon momentum: batch too large");
+  const int es = dtype == PO_BF16 ? 2 : 4;
+  const long long per_block = 256LL * (16 / es) * 4;  // four 16-byte vectors per thread
+  long long bx = (per + per_block - 1) / per_block;
+  const long long cap = (8LL * sm_count() + batch - 1) / batch;
+  if (bx > cap) bx = cap;
+  if (bx < 1) bx = 1;
+  dim3 grid(static_cast<unsigned>(bx), static_cast<unsigned>(batch));
+  const int vec = aligned16(g, buf, u) && (per * es) % 16 == 0;
+  if (dtype == PO_BF16)
+    momentum_sumsq_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(g), static_cast<__nv_bfloat16*>(buf), static_cast<__nv_bfloat16*>(u), per,
+        mu, nesterov, vec, sums);
+  else if (dtype == PO_F32)
+    momentum_sumsq_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(g), static_cast<float*>(buf),
+                                                      static_cast<float*>(u), per, mu, nesterov, vec, sums);
+  else
+    return set_error(PO_ERR_ARG, "muon momentum: dtype must be fp32 or bf16");
+  return check_cuda(cudaGetLastError(), "muon momentum launch");
+}
+
 }  // namespace po
 
 using namespace po;

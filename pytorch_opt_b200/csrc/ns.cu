@@ -2,12 +2,16 @@
 //
 // Mirrors pytorch_opt/ops/reference.py:71-97 (and the ATen version
 // pytorch_opt/ops/csrc/pytorch_opt_ops.cpp:65-81). Per matrix (m = min dim):
-//   pack   : X0 = G (transposed when rows > cols) / (||G||_F + eps)
+//   pack   : X0 = G / (||G||_F + eps), kept in G's orientation
 //   iterate: A = X X^T          (symmetric: lower tiles only, mirrored)
 //            B = b A + c A A    (symmetric: lower tiles only, A A = A A^T)
 //            X = a X + B X      (fp32 master copy of X updated in place)
-//   the last update writes the caller's output directly (transposed back,
-//   cast to the input dtype).
+//   the last update writes the caller's output directly (cast to its dtype).
+// Tall G (rows > cols): the reference transposes, iterates and transposes
+// back; since B is symmetric that equals iterating X (n x m) from the
+// right, A = X^T X, B = b A + c A A, X = a X + X B, which is what runs here:
+// no matrix is ever transposed, every epilogue access is row-contiguous, and
+// the update reads X K-major.
 //
 // Precision. All products accumulate in fp32. By default (m >= 256) every
 // step runs bf16 tensor-core products with the diagonal split: A and B have
@@ -48,15 +52,19 @@ struct NsBuffers {
   char* aop;                // A as product operand: fp32 (tf32) or bf16 hi | bf16 lo
   char* bop;                // B as product operand, same layout
   float* bdiag;             // diag(B) of the current step, fp32 [batch][m]
+  float* adiag;             // diag(A) of the current step, fp32 [batch][m]
+  float* scale;             // per matrix: 1 / (||G||_F + eps), then its square ([2][batch])
   double* sums;             // per-matrix sum of squares
   unsigned int* sched;      // tile queue of the products
   long long ldx, ldm, msz;  // msz: elements of one [batch][m][ldm] array
 };
 
-void ns_layout(Arena& ar, long long batch, long long m, long long n, bool split, NsBuffers& B) {
-  B.ldx = round_up(n, 64);
+// X is kept in G's orientation: [rows][ldx], ldx = cols rounded up to 64.
+void ns_layout(Arena& ar, long long batch, long long rows, long long cols, bool split, NsBuffers& B) {
+  const long long m = rows < cols ? rows : cols;
+  B.ldx = round_up(cols, 64);
   B.ldm = round_up(m, 64);
-  const size_t xs = static_cast<size_t>(batch * m * B.ldx);
+  const size_t xs = static_cast<size_t>(batch * rows * B.ldx);
   B.msz = batch * m * B.ldm;
   const size_t ms = static_cast<size_t>(B.msz);
   B.xf = static_cast<float*>(ar.take(xs * 4));
@@ -67,6 +75,8 @@ void ns_layout(Arena& ar, long long batch, long long m, long long n, bool split,
   B.aop = static_cast<char*>(ar.take(ms * 4));
   B.bop = static_cast<char*>(ar.take(ms * 4));
   B.bdiag = static_cast<float*>(ar.take(static_cast<size_t>(batch * m) * 4));
+  B.adiag = static_cast<float*>(ar.take(static_cast<size_t>(batch * m) * 4));
+  B.scale = static_cast<float*>(ar.take(static_cast<size_t>(batch) * 8));
   B.sums = static_cast<double*>(ar.take(static_cast<size_t>(batch) * 8));
   B.sched = take_sched(ar);
 }
@@ -126,7 +136,38 @@ void set_kind(GemmDesc& g, Prec pr) {
   g.chunked = pr == P_SPLIT;
 }
 
+// scale[b] = 1 / (sqrt(sums[b]) + eps), scale[batch + b] = scale[b]^2 (the
+// reference's pre-normalisation, reference.py:90, as a device-side factor).
+__global__ void ns_scale_kernel(const double* sums, float eps, float* scale, int batch) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  const float sc = 1.0f / (static_cast<float>(sqrt(sums[b])) + eps);
+  scale[b] = sc;
+  scale[batch + b] = sc * sc;
+}
+
 }  // namespace
+
+// Muon's in-place parameter update applied by the last product's epilogue
+// (see Epilogue::mu_p). p: [batch][rows][cols], pitch ld, batch pitch bs.
+struct NsApply {
+  void* p = nullptr;
+  int dtype = PO_BF16;
+  long long ld = 0, bs = 0;
+  float decay = 1.0f;
+  float lr_eff = 0.0f;
+  double* sq = nullptr;
+};
+
+struct NsOptions {
+  const double* sums = nullptr;  // per-matrix ||G||_F^2 already computed (nullable)
+  const NsApply* apply = nullptr;
+};
+
+int ns_core(const void* G, int dtype, long long batch, long long rows, long long cols, long long ld,
+            long long bstride, void* out, long long out_ld, long long out_bstride, int steps, float a, float b,
+            float c, float eps, int tf32_tail, void* workspace, size_t workspace_bytes, cudaStream_t s,
+            const NsOptions& opt);
 
 }  // namespace po
 
@@ -134,10 +175,10 @@ using namespace po;
 
 extern "C" size_t po_ns_workspace_bytes(long long batch, long long rows, long long cols) {
   if (batch <= 0 || rows <= 0 || cols <= 0) return 0;
-  const long long m = rows < cols ? rows : cols, n = rows < cols ? cols : rows;
+  const long long m = rows < cols ? rows : cols;
   Arena ar(nullptr, 0);
   NsBuffers B;
-  ns_layout(ar, batch, m, n, m < kSplitBelow, B);
+  ns_layout(ar, batch, rows, cols, m < kSplitBelow, B);
   return ar.used + 256;
 }
 
@@ -145,18 +186,36 @@ extern "C" int po_newton_schulz(const void* G, int dtype, long long batch, long 
                                 long long ld, long long bstride, void* out, long long out_ld, long long out_bstride,
                                 int steps, float a, float b, float c, float eps, int tf32_tail, void* workspace,
                                 size_t workspace_bytes, void* stream) {
+  return po::ns_core(G, dtype, batch, rows, cols, ld, bstride, out, out_ld, out_bstride, steps, a, b, c, eps,
+                     tf32_tail, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), po::NsOptions{});
+}
+
+namespace po {
+
+// The Newton-Schulz driver. With opt.sums the per-matrix squared norms are
+// given (the fused Muon step computes them with the momentum); with
+// opt.apply the last product updates the parameters in place (out, if not
+// null, still receives the orthogonalised matrix). When G is bf16 with
+// 16-byte aligned pitches and the step runs bf16 products, step 0 reads G
+// itself as its operands and addend (transposed views for tall matrices)
+// and applies the normalisation as device-side per-matrix factors of the
+// epilogues: no packed copy of G is made.
+int ns_core(const void* G, int dtype, long long batch, long long rows, long long cols, long long ld,
+            long long bstride, void* out, long long out_ld, long long out_bstride, int steps, float a, float b,
+            float c, float eps, int tf32_tail, void* workspace, size_t workspace_bytes, cudaStream_t s,
+            const NsOptions& opt) {
   if (dtype != PO_F32 && dtype != PO_BF16 && dtype != PO_F16 && dtype != PO_F64)
     return set_error(PO_ERR_ARG, "newton_schulz: dtype must be fp32, bf16, fp16 or fp64");
   if (batch < 0 || rows < 0 || cols < 0 || steps < 0)
     return set_error(PO_ERR_ARG, "newton_schulz: negative size or step count");
   if (batch == 0 || rows == 0 || cols == 0) return PO_OK;
-  if (G == nullptr || out == nullptr) return set_error(PO_ERR_ARG, "newton_schulz: null pointer");
-  if (ld < cols || out_ld < cols) return set_error(PO_ERR_ARG, "newton_schulz: row pitch smaller than cols");
+  if (G == nullptr || (out == nullptr && opt.apply == nullptr)) return set_error(PO_ERR_ARG, "newton_schulz: null pointer");
+  if (ld < cols || (out != nullptr && out_ld < cols))
+    return set_error(PO_ERR_ARG, "newton_schulz: row pitch smaller than cols");
   if (batch > 65535) return set_error(PO_ERR_ARG, "newton_schulz: batch too large (max 65535)");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
 
-  const bool trans = rows > cols;
-  const long long m = trans ? cols : rows, n = trans ? rows : cols;
+  const bool tall = rows > cols;
+  const long long m = tall ? cols : rows, n = tall ? rows : cols;
   if (m > 0x7fffffffLL / 2 || n > 0x7fffffffLL / 2) return set_error(PO_ERR_ARG, "newton_schulz: matrix too large");
   // Precision schedule.
   const bool split = tf32_tail < 0 && m < kSplitBelow;
@@ -166,43 +225,67 @@ extern "C" int po_newton_schulz(const void* G, int dtype, long long batch, long 
     if (split) return P_SPLIT;
     return it >= steps - tf32_tail ? P_TF32 : P_BF16;
   };
+  if (opt.apply != nullptr && steps == 0)
+    return set_error(PO_ERR_UNSUPPORTED, "newton_schulz: a fused update needs at least one step");
 
   Arena ar(workspace, workspace_bytes);
   NsBuffers B;
-  ns_layout(ar, batch, m, n, split, B);
+  ns_layout(ar, batch, rows, cols, split, B);
   if (workspace == nullptr || ar.overflow())
     return set_error(PO_ERR_WORKSPACE, "newton_schulz: workspace too small (query po_ns_workspace_bytes)");
 
-  int r = check_cuda(cudaMemsetAsync(B.sums, 0, static_cast<size_t>(batch) * 8, s), "memset");
-  if (r) return r;
+  int r;
   if ((r = zero_sched(B.sched, s))) return r;
   AnyMat src{G, dtype, rows, cols, ld, bstride};
-  if ((r = launch_sumsq(src, static_cast<int>(batch), B.sums, s))) return r;
+  const double* sums = opt.sums;
+  if (sums == nullptr) {
+    if ((r = check_cuda(cudaMemsetAsync(B.sums, 0, static_cast<size_t>(batch) * 8, s), "memset"))) return r;
+    if ((r = launch_sumsq(src, static_cast<int>(batch), B.sums, s))) return r;
+    sums = B.sums;
+  }
   const Prec p0 = prec_of(0);
-  if ((r = launch_ns_pack(src, static_cast<int>(batch), trans, B.sums, eps, B.xf,
-                          p0 == P_TF32 ? static_cast<void*>(B.xt[0]) : static_cast<void*>(B.xb[0]),
-                          p0 == P_SPLIT ? static_cast<void*>(B.xl[0]) : nullptr, p0 == P_TF32 ? OUT_TF32 : OUT_BF16,
-                          B.ldx, m, n, s)))
-    return r;
-  if (steps == 0)
-    return launch_copy_out(B.xf, B.ldx, m * B.ldx, static_cast<int>(batch), m, n, trans, out, dtype, out_ld,
-                           out_bstride, s);
+  const bool direct = dtype == PO_BF16 && p0 == P_BF16 && steps > 0 && reinterpret_cast<uintptr_t>(G) % 16 == 0 &&
+                      (ld * 2) % 16 == 0 && (batch == 1 || (bstride * 2) % 16 == 0);
+  if (direct) {
+    ns_scale_kernel<<<cdiv(batch, 128), 128, 0, s>>>(sums, eps, B.scale, static_cast<int>(batch));
+    if ((r = check_cuda(cudaGetLastError(), "ns scale"))) return r;
+  } else {
+    if ((r = launch_ns_pack(src, static_cast<int>(batch), false, sums, eps, B.xf,
+                            p0 == P_TF32 ? static_cast<void*>(B.xt[0]) : static_cast<void*>(B.xb[0]),
+                            p0 == P_SPLIT ? static_cast<void*>(B.xl[0]) : nullptr, p0 == P_TF32 ? OUT_TF32 : OUT_BF16,
+                            B.ldx, rows, cols, s)))
+      return r;
+    if (steps == 0)
+      return launch_copy_out(B.xf, B.ldx, rows * B.ldx, static_cast<int>(batch), rows, cols, false, out, dtype, out_ld,
+                             out_bstride, s);
+  }
 
-  const long long xs = m * B.ldx, ms = m * B.ldm;
+  const long long xs = rows * B.ldx, ms = m * B.ldm;
   // Operand arrays of A and B: fp32 for tf32 steps, else bf16 hi then bf16 lo.
   char* a_hi = B.aop;
   char* a_lo = B.aop + B.msz * 2;
   char* b_hi = B.bop;
   char* b_lo = B.bop + B.msz * 2;
+  // G itself as the step-0 operand and addend (X0 = G / ||G||).
+  MatView gv;
+  gv.ptr = G;
+  gv.dtype = PO_BF16;
+  gv.rows = rows;
+  gv.cols = cols;
+  gv.ld = ld;
+  gv.bstride = bstride;
   int cur = 0;
   for (int it = 0; it < steps; ++it) {
     const Prec pr = prec_of(it);
-    const OpView X = pr == P_TF32 ? op_view(pr, B.xt[cur], nullptr, m, n, B.ldx)
-                                  : op_view(pr, B.xb[cur], B.xl[cur], m, n, B.ldx);
+    const bool from_g = direct && it == 0;
+    OpView X = pr == P_TF32 ? op_view(pr, B.xt[cur], nullptr, rows, cols, B.ldx)
+                            : op_view(pr, B.xb[cur], B.xl[cur], rows, cols, B.ldx);
+    if (from_g) X.v[0] = X.v[1] = gv;
     const OpView Aop = op_view(pr, a_hi, a_lo, m, m, B.ldm);
     const OpView Bop = op_view(pr, b_hi, b_lo, m, m, B.ldm);
+    const bool ds = pr != P_SPLIT;  // diagonal split of the square and the update
 
-    // A = X X^T
+    // A = X X^T (wide: X K-major), or X^T X (tall: X read MN-major).
     GemmDesc g;
     set_kind(g, pr);
     g.M = g.N = static_cast<int>(m);
@@ -210,6 +293,8 @@ extern "C" int po_newton_schulz(const void* G, int dtype, long long batch, long 
     g.batch = static_cast<int>(batch);
     g.a[0] = X.v[0]; g.a[1] = X.v[1];
     g.b[0] = X.v[0]; g.b[1] = X.v[1];
+    g.a_kmajor = g.b_kmajor = !tall;
+    if (from_g) g.epi.alpha_scale = B.scale + batch;  // (G / ||G||) Gram = s^2 (G Gram)
     g.tri = true;
     g.sched = B.sched;
     g.epi.alpha = 1.0f;
@@ -219,7 +304,10 @@ extern "C" int po_newton_schulz(const void* G, int dtype, long long batch, long 
     g.pair = gemm_uses_pair(g) ? 1 : 0;
     g.epi.out[g.epi.nout] = epi_out(B.af, OUT_F32, B.ldm, ms);
     g.epi.out[g.epi.nout++].lower_only = 1;
-    const bool ds = pr != P_SPLIT;  // diagonal split of the square and the update
+    if (ds) {
+      g.epi.diag_out = B.adiag;
+      g.epi.diag_out_bs = m;
+    }
     add_op_outputs(g.epi, pr, a_hi, a_lo, B.ldm, ms, ds);
     if ((r = launch_gemm(g, s))) return r;
 
@@ -238,34 +326,57 @@ extern "C" int po_newton_schulz(const void* G, int dtype, long long batch, long 
     q.epi.nin = 1;
     q.epi.in[0] = epi_in(B.af, IN_F32, B.ldm, ms, b);
     if (ds) {
-      // A A = F F + D A + A D - D^2 with F (the operands) zero on the diagonal.
-      q.epi.diag_split = 1;
-      q.epi.dU = epi_in(B.af, IN_F32, B.ldm, ms, 1.0f);
-      q.epi.dV = q.epi.dU;
+      // A A = F F + D A + A D - D^2 with F (the operands) zero on the diagonal,
+      // D = diag(A) as the Gram wrote it; one row read of A.
+      q.epi.dsym = B.adiag;
+      q.epi.dsym_bs = m;
       q.epi.diag_out = B.bdiag;
       q.epi.diag_out_bs = m;
     }
     add_op_outputs(q.epi, pr, b_hi, b_lo, B.ldm, ms, ds);
     if ((r = launch_gemm(q, s))) return r;
 
-    // X = a X + B X ; B operand is X stored [K = m][N = n] (MN-major).
+    // Wide: X = a X + B X (B operand X stored [K = m][N = n], MN-major).
+    // Tall: X = a X + X B (A operand X [n][K = m], K-major; B symmetric).
     GemmDesc u;
     set_kind(u, pr);
-    u.M = static_cast<int>(m);
-    u.N = static_cast<int>(n);
-    u.K = static_cast<int>(m);
     u.batch = static_cast<int>(batch);
-    u.a[0] = Bop.v[0]; u.a[1] = Bop.v[1];
-    u.b[0] = X.v[0]; u.b[1] = X.v[1];
-    u.b_kmajor = false;
+    u.K = static_cast<int>(m);
+    if (tall) {
+      u.M = static_cast<int>(n);
+      u.N = static_cast<int>(m);
+      u.a[0] = X.v[0]; u.a[1] = X.v[1];
+      u.b[0] = Bop.v[0]; u.b[1] = Bop.v[1];
+      u.a_kmajor = true;
+      u.b_kmajor = true;
+    } else {
+      u.M = static_cast<int>(m);
+      u.N = static_cast<int>(n);
+      u.a[0] = Bop.v[0]; u.a[1] = Bop.v[1];
+      u.b[0] = X.v[0]; u.b[1] = X.v[1];
+      u.b_kmajor = false;
+    }
     u.sched = B.sched;
     u.epi.alpha = 1.0f;
     u.epi.nin = 1;
-    u.epi.in[0] = epi_in(B.xf, IN_F32, B.ldx, xs, a);
+    if (from_g) {
+      // s (B G or G B) + s (a + B_jj) G: both terms scaled by s = 1 / ||G||.
+      u.epi.alpha_scale = B.scale;
+      u.epi.in_scale = B.scale;
+      u.epi.in[0] = epi_in(G, IN_BF16, ld, bstride, a);
+    } else {
+      u.epi.in[0] = epi_in(B.xf, IN_F32, B.ldx, xs, a);
+    }
     if (ds) {
-      // B X = F_B X + diag(B) X: the fp32 addend X is scaled by a + B_ii.
-      u.epi.in0_rowcoef = B.bdiag;
-      u.epi.in0_rowcoef_bs = m;
+      // The dominant diagonal of B goes to the addend exactly: B X = F_B X +
+      // diag(B) X (row scale a + B_ii) or X B = X F_B + X diag(B) (column scale).
+      if (tall) {
+        u.epi.in0_colcoef = B.bdiag;
+        u.epi.in0_colcoef_bs = m;
+      } else {
+        u.epi.in0_rowcoef = B.bdiag;
+        u.epi.in0_rowcoef_bs = m;
+      }
     }
     if (it + 1 < steps) {
       const Prec pn = prec_of(it + 1);
@@ -274,10 +385,85 @@ extern "C" int po_newton_schulz(const void* G, int dtype, long long batch, long 
       if (pn == P_TF32) add_op_outputs(u.epi, pn, B.xt[nxt], nullptr, B.ldx, xs);
       else add_op_outputs(u.epi, pn, B.xb[nxt], B.xl[nxt], B.ldx, xs);
     } else {
-      u.epi.out[u.epi.nout++] = epi_out(out, out_kind_of(dtype), out_ld, out_bstride, trans);
+      if (out != nullptr) u.epi.out[u.epi.nout++] = epi_out(out, out_kind_of(dtype), out_ld, out_bstride);
+      if (opt.apply != nullptr) {
+        const NsApply& ap = *opt.apply;
+        u.epi.mu_p = ap.p;
+        u.epi.mu_ld = ap.ld;
+        u.epi.mu_bs = ap.bs;
+        u.epi.mu_bf16 = ap.dtype == PO_BF16 ? 1 : 0;
+        const int es = ap.dtype == PO_BF16 ? 2 : 4;
+        u.epi.mu_vec = reinterpret_cast<uintptr_t>(ap.p) % 16 == 0 && (ap.ld * es) % 16 == 0 && (ap.bs * es) % 16 == 0;
+        u.epi.mu_use_decay = ap.decay != 1.0f;
+        u.epi.mu_decay = ap.decay;
+        // add_(O, alpha=-lr_eff) on a bf16 tensor rounds alpha to bf16 first.
+        u.epi.mu_alpha = ap.dtype == PO_BF16 ? __bfloat162float(__float2bfloat16_rn(-ap.lr_eff)) : -ap.lr_eff;
+        u.epi.red_sumsq = ap.sq;
+        u.epi.red_sumsq_shared = 1;
+      }
     }
     if ((r = launch_gemm(u, s))) return r;
     cur ^= 1;
   }
   return PO_OK;
+}
+
+}  // namespace po
+
+using namespace po;
+
+extern "C" size_t po_muon_step_workspace_bytes(long long batch, long long rows, long long cols, int dtype) {
+  if (batch <= 0 || rows <= 0 || cols <= 0) return 0;
+  const long long es = dtype == PO_BF16 ? 2 : 4;
+  return static_cast<size_t>(round_up(batch * rows * cols * es, 256) + round_up(batch * 8, 256)) +
+         po_ns_workspace_bytes(batch, rows, cols) + 256;
+}
+
+extern "C" int po_muon_step(const void* g, void* buf, void* p, int dtype, long long batch, long long rows,
+                            long long cols, float momentum, int nesterov, int ns_steps, float a, float b, float c,
+                            float eps, float lr_eff, float decay, double* sq_sum, void* o_out, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (dtype != PO_BF16 && dtype != PO_F32) return set_error(PO_ERR_ARG, "muon_step: dtype must be fp32 or bf16");
+  if (batch < 0 || rows < 0 || cols < 0 || ns_steps < 0) return set_error(PO_ERR_ARG, "muon_step: negative size");
+  if (batch == 0 || rows == 0 || cols == 0) return PO_OK;
+  if (!g || !buf || !p) return set_error(PO_ERR_ARG, "muon_step: null pointer");
+  if (batch > 65535) return set_error(PO_ERR_ARG, "muon_step: batch too large (max 65535)");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const long long per = rows * cols, es = dtype == PO_BF16 ? 2 : 4;
+  Arena ar(workspace, workspace_bytes);
+  void* u = ar.take(static_cast<size_t>(batch * per * es));
+  auto* sums = static_cast<double*>(ar.take(static_cast<size_t>(batch) * 8));
+  const size_t ns_bytes = po_ns_workspace_bytes(batch, rows, cols);
+  void* ns_ws = ar.take(ns_bytes);
+  if (workspace == nullptr || ar.overflow())
+    return set_error(PO_ERR_WORKSPACE, "muon_step: workspace too small (query po_muon_step_workspace_bytes)");
+  int r = check_cuda(cudaMemsetAsync(sums, 0, static_cast<size_t>(batch) * 8, s), "memset");
+  if (r) return r;
+  if ((r = launch_momentum_sumsq(g, buf, u, dtype, batch, per, momentum, nesterov, sums, s))) return r;
+  if (ns_steps == 0) {
+    // O is the normalised u itself: write it over u, then the separate update pass.
+    NsOptions opt;
+    opt.sums = sums;
+    if ((r = ns_core(u, dtype, batch, rows, cols, cols, per, u, cols, per, 0, a, b, c, eps, -1, ns_ws, ns_bytes, s,
+                     opt)))
+      return r;
+    if (o_out != nullptr &&
+        (r = check_cuda(cudaMemcpyAsync(o_out, u, static_cast<size_t>(batch * per * es), cudaMemcpyDeviceToDevice, s),
+                        "copy")))
+      return r;
+    return po_muon_apply(p, u, dtype, batch * per, lr_eff, decay, sq_sum, stream);
+  }
+  NsApply ap;
+  ap.p = p;
+  ap.dtype = dtype;
+  ap.ld = cols;
+  ap.bs = per;
+  ap.decay = decay;
+  ap.lr_eff = lr_eff;
+  ap.sq = sq_sum;
+  NsOptions opt;
+  opt.sums = sums;
+  opt.apply = &ap;
+  return ns_core(u, dtype, batch, rows, cols, cols, per, o_out, cols, per, ns_steps, a, b, c, eps, -1, ns_ws,
+                 ns_bytes, s, opt);
 }

@@ -21,6 +21,7 @@ enum DeviceError : int {
   kErrTimeoutMma = 2,        // MMA issuer waited too long for operands / TMEM
   kErrTimeoutEpilogue = 3,   // epilogue waited too long for an accumulator
   kErrTimeoutDrain = 4,      // teardown waited too long for in-flight work
+  kErrTimeoutSelfTest = 5,   // po_selftest_wait_timeout: a wait on a barrier nothing arms
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -65,17 +66,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Wait for the phase with the given parity to complete. Returns false when
 // the CTA-wide abort flag is raised (by this or another role) or when the
-// wait exceeds kWaitTimeoutNs; in the latter case the abort flag is raised
-// and `code` is recorded in *err (first error wins).
+// wait exceeds limit_ns (kWaitTimeoutNs); in the latter case the abort flag
+// is raised and `code` is recorded in *err (first error wins).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                                  int* err, int code) {
+                                                  int* err, int code,
+                                                  unsigned long long limit_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 31u) == 0) {
       if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+      if (global_timer_ns() - t0 > limit_ns) {
         *abort_flag = 1;
         atomicCAS(err, 0, code);
         return false;
@@ -102,13 +104,14 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 // whole main loop for its accumulator): sleeps in the barrier, with the same
 // timeout and abort semantics as mbar_wait_bounded.
 __device__ __forceinline__ bool mbar_wait_bounded_sleep(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                                        int* err, int code) {
+                                                        int* err, int code,
+                                                        unsigned long long limit_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   for (;;) {
     if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+    if (global_timer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       atomicCAS(err, 0, code);
       return false;
@@ -265,14 +268,15 @@ __device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uin
 }
 // Bounded wait whose release side may be in the peer CTA.
 __device__ __forceinline__ bool mbar_wait_bounded_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                                          int* err, int code) {
+                                                          int* err, int code,
+                                                          unsigned long long limit_ns = kWaitTimeoutNs) {
   if (mbar_try_wait_acq_cluster(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait_acq_cluster(bar, parity)) return true;
     if ((i & 31u) == 0) {
       if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+      if (global_timer_ns() - t0 > limit_ns) {
         *abort_flag = 1;
         atomicCAS(err, 0, code);
         return false;

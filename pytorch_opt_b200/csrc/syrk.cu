@@ -109,6 +109,7 @@ int syrk_update(float* F, long long f_ld, const Operand& op, bool gram_of_rows, 
   g.epi.nout = 1;
   g.epi.out[0] = epi_out(F, OUT_F32, f_ld, d * f_ld);
   g.epi.red_trace = trace;
+  g.epi.sym_diag = op.npass > 1 ? 1 : 0;  // split passes: make diagonal tiles bit-symmetric
   return launch_gemm(g, s);
 }
 

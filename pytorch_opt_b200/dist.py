@@ -66,12 +66,33 @@ class _Group:
     flat: int = 0       # element offset of the group in the flat buffer
 
 
+def chunk_shares(chunks: int) -> list[float]:
+    """FLOP share of each exchange chunk, decreasing (e.g. 4: 0.40, 0.30, 0.22,
+    0.08): the last chunk's all-gather cannot overlap anything, so it is kept
+    small, while each earlier chunk's gather hides behind the larger compute
+    of the chunks after it."""
+    if chunks <= 1:
+        return [1.0]
+    w = [float(chunks - c) for c in range(chunks)]
+    w[-1] *= 0.5
+    t = sum(w)
+    return [x / t for x in w]
+
+
+def bytes_per_flop(rows: int, cols: int) -> float:
+    """Exchanged bytes (bf16) per Newton–Schulz FLOP of a matrix: ~1/(10 min dim)."""
+    return 2.0 * rows * cols / ns_flops(rows, cols)
+
+
 class ShardLayout:
     """Placement of matrices in a flat parameter buffer, sharded by rank and chunk.
 
-    Each rank's matrices (LPT plan) are cut, in processing order, into
-    ``chunks`` runs of about equal Newton–Schulz FLOPs; inside a run they are
-    grouped by shape. The flat buffer is ``[chunk][world][chunk_len[chunk]]``:
+    Each rank's matrices (LPT plan) are processed in decreasing order of
+    exchanged bytes per FLOP (Llama: k/v, then gate/up/down, then q/o) and cut
+    into ``chunks`` runs whose FLOP shares decrease (``chunk_shares``), so the
+    last chunk — whose all-gather is exposed — is small and made of the
+    matrices with the fewest bytes per FLOP; inside a run they are grouped by
+    shape. The flat buffer is ``[chunk][world][chunk_len[chunk]]``:
     chunk c of every rank sits side by side, so chunk c's exchange is one
     ``all_gather_into_tensor`` whose output is a contiguous slice of the
     buffer, and it can start as soon as every rank has stepped its chunk c
@@ -91,13 +112,19 @@ class ShardLayout:
         self.chunks = max(1, int(chunks))
         # Per rank: matrices in processing order (largest shapes first), cut into chunk runs.
         runs: list[list[list[int]]] = []
+        edges = []
+        acc_share = 0.0
+        for sh in chunk_shares(self.chunks):
+            acc_share += sh
+            edges.append(acc_share)
         for r in range(world):
-            mine = sorted(self.assign[r], key=lambda i: (-self.shapes[i][0] * self.shapes[i][1], self.shapes[i], i))
+            mine = sorted(self.assign[r], key=lambda i: (-bytes_per_flop(*self.shapes[i]), self.shapes[i], i))
             total = sum(costs[i] for i in mine)
             parts: list[list[int]] = [[] for _ in range(self.chunks)]
             acc = 0.0
             for i in mine:
-                c = min(self.chunks - 1, int(acc * self.chunks / total)) if total > 0 else 0
+                mid = (acc + 0.5 * costs[i]) / total if total > 0 else 0.0  # chunk of the matrix's midpoint
+                c = next((k for k, e in enumerate(edges) if mid < e), self.chunks - 1)
                 parts[c].append(i)
                 acc += costs[i]
             runs.append(parts)
@@ -213,7 +240,7 @@ class ShardedMuon:
         self._sq = torch.zeros(max(len(self.groups), 1), dtype=torch.float64, device=params_flat.device)
         self._ws = None
         if compute is None and self.groups:
-            need = max(ns_workspace_bytes(*g.params.shape) for g in self.groups)
+            need = max(ns_workspace_bytes(*g.params.shape, dtype=g.params.dtype) for g in self.groups)
             self._ws = torch.empty(need, dtype=torch.uint8, device=params_flat.device)
 
     def _step_group(self, k: int, ns_events: list | None) -> None:
@@ -327,7 +354,7 @@ class ShardedMuon:
         total = 0
         for g in self.groups:
             count = g.params.shape[0] if self.compute is None else g[0].shape[0]
-            total += 2 + (-(-count // 32)) * (2 + 3 * int(self.hp["ns_steps"]))
+            total += (-(-count // 32)) * (2 + 3 * int(self.hp["ns_steps"]))
         return total
 
     def local_update_sq(self) -> float:
@@ -396,6 +423,32 @@ def _band_product(band: torch.Tensor, X: torch.Tensor, r0: int, r1: int, alpha: 
                "po_matmul")
 
 
+def band_update_(D: torch.Tensor, F: torch.Tensor, X: torch.Tensor, alpha: float, beta: float, first: bool, r0: int,
+                 r1: int, compute=None) -> None:
+    """One rank's band of the factor update: rows [r0, r1) x columns [0, r1) of
+    ``first ? alpha X^T X : beta F + (1 - beta) alpha X^T X`` written into the
+    same rows and columns of ``D`` (d x d fp32, or a band-shaped view whose
+    row r0 is its first row when ``D.shape[0] == r1 - r0``)."""
+    if r1 <= r0:
+        return
+    band = D[r0:r1, :r1] if D.shape[0] == F.shape[0] else D[:r1 - r0, :r1]
+    if first:
+        band.zero_()  # products called with beta = 0 must not see stale values (0 * NaN)
+    else:
+        band.copy_(F[r0:r1, :r1])
+    a_eff = alpha if first else (1.0 - beta) * alpha
+    b_eff = 0.0 if first else beta
+    (compute or _band_product)(band, X, r0, r1, a_eff, b_eff)
+
+
+def mirror_lower_(F: torch.Tensor, D: torch.Tensor) -> torch.Tensor:
+    """F <- the symmetric matrix whose lower triangle is D's."""
+    return F.copy_(torch.tril(D) + torch.tril(D, -1).mT)
+
+
+_GATHER_BUFFERS: dict = {}
+
+
 def sharded_syrk_ema_(F: torch.Tensor, X: torch.Tensor, alpha: float, beta: float, first: bool, rank: int = 0,
                       world: int = 1, group=None, compute=None) -> torch.Tensor:
     """KFAC factor update ``F <- first ? alpha X^T X : beta F + (1 - beta) alpha X^T X`` split across ranks.
@@ -403,30 +456,41 @@ def sharded_syrk_ema_(F: torch.Tensor, X: torch.Tensor, alpha: float, beta: floa
     The statistic of ``pytorch_opt/curvature/kron.py:95-113`` for one layer,
     with its d x d output cut into row bands of equal work
     (``kfac_band_bounds``): every rank holds the same ``F`` (fp32) and ``X``
-    (rows x d, fp32 or bf16), computes only its band on the tensor cores,
-    one ``all_reduce`` assembles the lower triangle, and each rank mirrors it
-    into the full symmetric ``F``. With ``world == 1`` it is one product over
-    the whole matrix. ``compute(band, X, r0, r1, alpha, beta)`` replaces the
-    tensor-core product (host-side tests over gloo).
+    (rows x d, fp32 or bf16), computes only its band on the tensor cores, the
+    bands are exchanged with one ``all_gather_into_tensor`` from a cached
+    ``[max band][d]`` band into a cached ``[world][max band][d]`` buffer (each
+    rank receives the lower triangle once), and each rank mirrors it into the
+    full symmetric ``F``. With
+    ``world == 1`` the fused triangular SYRK+EMA kernel does the whole update.
+    ``compute(band, X, r0, r1, alpha, beta)`` replaces the tensor-core
+    product (host-side tests over gloo).
     """
     if X.dim() != 2 or F.dim() != 2 or F.shape[0] != F.shape[1] or F.shape[0] != X.shape[1]:
         raise RuntimeError("sharded_syrk_ema_: expects X (rows, d) and F (d, d)")
     if F.dtype != torch.float32 or not F.is_contiguous():
         raise RuntimeError("sharded_syrk_ema_: F must be a contiguous fp32 tensor")
     d = F.shape[0]
+    if world == 1 and compute is None:
+        from . import native
+        return native.kron_syrk_ema_(F, X, alpha, beta, first)
     bounds = kfac_band_bounds(d, world)
     r0, r1 = bounds[rank], bounds[rank + 1]
+    hmax = max(bounds[k + 1] - bounds[k] for k in range(world))
     Xw = (X if X.dtype in (torch.float32, torch.bfloat16) else X.float()).contiguous()
-    D = torch.zeros_like(F)
-    if r1 > r0:
-        band = D[r0:r1, :r1]
-        if not first:
-            band.copy_(F[r0:r1, :r1])
-        a_eff = alpha if first else (1.0 - beta) * alpha
-        b_eff = 0.0 if first else beta
-        (compute or _band_product)(band, Xw, r0, r1, a_eff, b_eff)
+    key = (F.device, d, world, hmax)
+    bufs = _GATHER_BUFFERS.get(key)
+    if bufs is None:  # the band (input) and the gathered bands (output), reused across calls
+        bufs = _GATHER_BUFFERS[key] = (torch.empty(hmax, d, dtype=torch.float32, device=F.device),
+                                       torch.empty(world, hmax, d, dtype=torch.float32, device=F.device))
+    mine, buf = bufs
+    band_update_(mine, F, Xw, alpha, beta, first, r0, r1, compute)
     if world > 1:
-        dist.all_reduce(D, group=group)
-    F.copy_(torch.tril(D) + torch.tril(D, -1).mT)
-    return F
-
+        dist.all_gather_into_tensor(buf.view(-1), mine.view(-1), group=group)
+    else:
+        buf[0].copy_(mine)
+    D = F  # assemble the lower triangle in place, then mirror it
+    for k in range(world):
+        a, b = bounds[k], bounds[k + 1]
+        if b > a:
+            D[a:b, :b] = buf[k, :b - a, :b]
+    return mirror_lower_(F, D)

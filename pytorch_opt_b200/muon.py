@@ -4,13 +4,16 @@ The reference updates one matrix at a time (``pytorch_opt/optim/muon.py:70-98``)
 momentum, Nesterov, Newton–Schulz, spectral scale, weight decay, update, and a
 host sync per matrix for the ``update_rms`` diagnostic (:92). Here matrices
 of equal shape live in one ``[count, rows, cols]`` tensor and are stepped
-together: one momentum launch, one batched Newton–Schulz (15 tensor-core
-launches for five steps), one update launch per shape group, and the
-diagnostic's sum of squares accumulates on the device.
+together by ``po_muon_step``: per call of up to 32 matrices, one momentum
+pass that also sums each matrix's squared norm, one tiny scale kernel and
+the 15 tensor-core products of five Newton–Schulz steps, the last of which
+updates the parameters in its epilogue; the diagnostic's sum of squares
+accumulates on the device.
 """
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass, field
 
 import torch
@@ -42,6 +45,7 @@ class MuonGroup:
     params: torch.Tensor
     grads: torch.Tensor
     momentum: torch.Tensor = None
+    keep_update: bool = False  # also store the orthogonalised update O in ``_u`` (tests, diagnostics)
     _u: torch.Tensor = field(default=None, repr=False)
     _ws: torch.Tensor = field(default=None, repr=False)
 
@@ -58,9 +62,9 @@ class MuonGroup:
             self.momentum = torch.zeros_like(self.params)
 
 
-def ns_workspace_bytes(count: int, rows: int, cols: int, max_batch: int = 32) -> int:
-    """Workspace one ``muon_group_step`` call needs (Newton–Schulz on up to ``max_batch`` matrices)."""
-    return int(_lib.load().po_ns_workspace_bytes(min(count, max_batch), rows, cols))
+def ns_workspace_bytes(count: int, rows: int, cols: int, max_batch: int = 32, dtype=torch.bfloat16) -> int:
+    """Workspace one ``muon_group_step`` call needs (fused steps of up to ``max_batch`` matrices)."""
+    return int(_lib.load().po_muon_step_workspace_bytes(min(count, max_batch), rows, cols, _lib.DTYPE_CODE[dtype]))
 
 
 def muon_group_step(group: MuonGroup, lr: float = 0.02, momentum: float = 0.95, nesterov: bool = True,
@@ -73,54 +77,78 @@ def muon_group_step(group: MuonGroup, lr: float = 0.02, momentum: float = 0.95, 
     orthogonalised updates (the reference's ``update_rms`` numerator before
     the ``eff^2`` factor). ``workspace``: optional uint8 CUDA buffer of at
     least ``ns_workspace_bytes`` (shared between groups stepped on one
-    stream); Newton–Schulz runs on at most ``max_batch`` matrices per call to
+    stream); the fused step runs on at most ``max_batch`` matrices per call to
     bound it. ``ns_events``: optional list; a (start, end) pair of CUDA events
-    recorded around the Newton–Schulz launches is appended (for timing).
+    recorded around the group's fused steps is appended (for timing).
     """
     lib = _lib.load()
     p = group.params
     count, rows, cols = p.shape
-    n = p.numel()
-    if n == 0:
+    if p.numel() == 0:
         return
     dev = p.device
     code = _lib.DTYPE_CODE[p.dtype]
     stream = _lib.stream_ptr(dev)
-    if group._u is None:
-        group._u = torch.empty_like(p)
     nb = min(count, max_batch)
-    nbytes = lib.po_ns_workspace_bytes(nb, rows, cols)
+    nbytes = lib.po_muon_step_workspace_bytes(nb, rows, cols, code)
     if workspace is None:
         if group._ws is None or group._ws.numel() < nbytes:
             group._ws = _lib.workspace(nbytes, dev)
         workspace = group._ws
     elif workspace.numel() < nbytes:
         raise ValueError(f"workspace too small: {workspace.numel()} < {nbytes} bytes")
-    u = group._u
+    if group.keep_update and group._u is None:
+        group._u = torch.empty_like(p)
     mat = rows * cols
     es = p.element_size()
+    a, b, c = coeffs
+    eff = lr * muon_scale(rows, cols, lr_adjust)
+    decay = 1.0 - lr * weight_decay if weight_decay else 1.0
+    sq_ptr = sq_sum.data_ptr() if sq_sum is not None else None
+    # Measurement switch: PO_MUON_FUSED=0 runs the unfused calls (momentum,
+    # Newton-Schulz on a packed copy, update) for A/B timing of the fused step.
+    unfused = os.environ.get("PO_MUON_FUSED", "1") == "0"
     with torch.cuda.device(dev):
-        _lib.check(lib.po_muon_momentum(group.grads.data_ptr(), group.momentum.data_ptr(), u.data_ptr(), code, n,
-                                        float(momentum), 1 if nesterov else 0, stream), "po_muon_momentum")
-        a, b, c = coeffs
-        # The orthogonalised update overwrites u in place: Newton–Schulz reads its
-        # input only in the packing pass that precedes every product.
         if ns_events is not None:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record()
-        for start in range(0, count, max_batch):
+        if unfused:
+            _unfused_group_step(lib, group, code, stream, workspace, momentum, nesterov, ns_steps, coeffs, eps, eff,
+                                decay, sq_ptr, max_batch)
+        for start in range(0, count if not unfused else 0, max_batch):
             k = min(max_batch, count - start)
-            ptr = u.data_ptr() + start * mat * es
-            _lib.check(lib.po_newton_schulz(ptr, code, k, rows, cols, cols, mat, ptr, cols, mat, int(ns_steps),
-                                            float(a), float(b), float(c), float(eps), -1, workspace.data_ptr(),
-                                            workspace.numel(), stream), "po_newton_schulz")
+            off = start * mat * es
+            o_ptr = group._u.data_ptr() + off if group.keep_update else None
+            _lib.check(lib.po_muon_step(group.grads.data_ptr() + off, group.momentum.data_ptr() + off,
+                                        p.data_ptr() + off, code, k, rows, cols, float(momentum),
+                                        1 if nesterov else 0, int(ns_steps), float(a), float(b), float(c), float(eps),
+                                        float(eff), float(decay), sq_ptr, o_ptr, workspace.data_ptr(),
+                                        workspace.numel(), stream), "po_muon_step")
         if ns_events is not None:
             ev1.record()
             ns_events.append((ev0, ev1))
-        eff = lr * muon_scale(rows, cols, lr_adjust)
-        decay = 1.0 - lr * weight_decay if weight_decay else 1.0
-        _lib.check(lib.po_muon_apply(p.data_ptr(), u.data_ptr(), code, n, float(eff), float(decay),
-                                     sq_sum.data_ptr() if sq_sum is not None else None, stream), "po_muon_apply")
+
+
+def _unfused_group_step(lib, group, code, stream, workspace, momentum, nesterov, ns_steps, coeffs, eps, eff, decay,
+                        sq_ptr, max_batch):
+    p = group.params
+    count, rows, cols = p.shape
+    if group._u is None:
+        group._u = torch.empty_like(p)
+    u = group._u
+    mat = rows * cols
+    es = p.element_size()
+    a, b, c = coeffs
+    _lib.check(lib.po_muon_momentum(group.grads.data_ptr(), group.momentum.data_ptr(), u.data_ptr(), code, p.numel(),
+                                    float(momentum), 1 if nesterov else 0, stream), "po_muon_momentum")
+    for start in range(0, count, max_batch):
+        k = min(max_batch, count - start)
+        ptr = u.data_ptr() + start * mat * es
+        _lib.check(lib.po_newton_schulz(ptr, code, k, rows, cols, cols, mat, ptr, cols, mat, int(ns_steps), float(a),
+                                        float(b), float(c), float(eps), -1, workspace.data_ptr(), workspace.numel(),
+                                        stream), "po_newton_schulz")
+    _lib.check(lib.po_muon_apply(p.data_ptr(), u.data_ptr(), code, p.numel(), float(eff), float(decay), sq_ptr, stream),
+               "po_muon_apply")
 
 
 class GroupedMuon:
@@ -137,7 +165,7 @@ class GroupedMuon:
         # One fp64 accumulator of sum(O^2) per group (groups differ in eff).
         self._sq = torch.zeros(max(len(groups), 1), dtype=torch.float64, device=dev)
         # Groups run one after another on one stream: they share one workspace.
-        need = max((ns_workspace_bytes(*g.params.shape) for g in groups), default=1)
+        need = max((ns_workspace_bytes(*g.params.shape, dtype=g.params.dtype) for g in groups), default=1)
         self._ws = _lib.workspace(need, dev)
 
     def step(self) -> None:
@@ -146,11 +174,12 @@ class GroupedMuon:
             muon_group_step(g, sq_sum=self._sq[i], workspace=self._ws, **self.hp)
 
     def launches_per_step(self) -> int:
-        """Kernels this library launches per ``step()`` (momentum, NS packing + products, update)."""
+        """Kernels this library launches per ``step()``: per fused call of up to 32
+        matrices, the momentum pass, the scale (or packing) kernel and the products."""
         total = 0
         for g in self.groups:
             chunks = -(-g.params.shape[0] // 32)
-            total += 2 + chunks * (2 + 3 * int(self.hp["ns_steps"]))
+            total += chunks * (2 + 3 * int(self.hp["ns_steps"]))
         return total
 
     def update_rms(self) -> float:

@@ -53,6 +53,25 @@ def test_native_library_is_the_in_tree_build(cuda):
     assert torch.cuda.get_device_capability(cuda)[0] == 10
 
 
+@pytest.mark.parametrize("sleeping", [0, 1])
+def test_bounded_wait_gives_up_and_reports(cuda, sleeping):
+    """A kernel wait on a barrier nothing arms ends after its limit (20 ms
+    here instead of 5 s): the kernel returns, po_device_error() reports code
+    5 once, and the context keeps working (a product runs afterwards)."""
+    import time
+    lib = _lib.load()
+    assert _lib.device_error(reset=True) == 0
+    t0 = time.perf_counter()
+    _lib.check(lib.po_selftest_wait_timeout(20_000_000, sleeping, _lib.stream_ptr(cuda)), "selftest")
+    code = _lib.device_error(reset=True)
+    took = time.perf_counter() - t0
+    assert code == 5, code
+    assert took < 5.0, took
+    assert _lib.device_error(reset=True) == 0  # reset clears it
+    G = torch.randn(64, 96, device=cuda)
+    assert _rel(_np(ops.newton_schulz_orthogonalize(G)), O.newton_schulz(_np(G))) <= NS_TOL
+
+
 # ---------------------------------------------------------------- Newton–Schulz
 
 def test_ns_golden(cuda):
@@ -257,6 +276,34 @@ def test_band_split_factor_update_one_rank(cuda, dt):
     assert torch.equal(Fa, Fa.T)
 
 
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_band_split_all_bands_one_gpu(cuda, dt, world):
+    """Every band of a world-rank split computed on one GPU (no NCCL): offset
+    A operand (X + r0, transposed), band width r1 < d, the EMA epilogue on a
+    band view; assembled and mirrored, against the fused kernel and the oracle."""
+    from pytorch_opt_b200.dist import band_update_, kfac_band_bounds, mirror_lower_
+    g = torch.Generator().manual_seed(31 + world)
+    rows, d = 1024, 700  # d not a multiple of 16
+    X1 = torch.randn(rows, d, generator=g).to(dt)
+    X2 = torch.randn(rows, d, generator=g).to(dt)
+    bounds = kfac_band_bounds(d, world)
+    Fa = torch.empty(d, d, device=cuda)
+    Fb = torch.empty(d, d, device=cuda)
+    for X, first in ((X1, True), (X2, False)):
+        Xc = X.to(cuda).contiguous()
+        D = torch.zeros(d, d, device=cuda)
+        for k in range(world):
+            band_update_(D, Fa, Xc, 1.0 / rows, 0.95, first, bounds[k], bounds[k + 1])
+        mirror_lower_(Fa, D)
+        native.kron_syrk_ema_(Fb, Xc, 1.0 / rows, 0.95, first)
+    assert _rel(_np(Fa), _np(Fb).astype(np.float64)) <= 1e-5
+    x1, x2 = _np(X1).astype(np.float64), _np(X2).astype(np.float64)
+    want = 0.95 * (x1.T @ x1 / rows) + 0.05 * (x2.T @ x2 / rows)
+    assert _rel(_np(Fa), want) <= FACTOR_TOL
+    assert torch.equal(Fa, Fa.T)
+
+
 def test_kfac_golden_factors_and_inverse(cuda):
     """Golden KronTracker factors (ghat = n g) and the damped inverse by the Newton kernel."""
     z = np.load(os.path.join(GOLDEN_DIR, "kfac.npz"))
@@ -386,7 +433,7 @@ def test_grouped_muon_vs_oracle_gpt2_shapes(cuda):
         g = torch.Generator().manual_seed(shp[1])
         p0 = (torch.randn(2, *shp, generator=g) * 0.02).bfloat16()
         gr = (torch.randn(2, *shp, generator=g) * 0.02).bfloat16()
-        grp = MuonGroup(p0.clone().to(cuda), gr.clone().to(cuda))
+        grp = MuonGroup(p0.clone().to(cuda), gr.clone().to(cuda), keep_update=True)
         GroupedMuon([grp], lr=0.02, weight_decay=0.01).step()
         for b in range(2):
             _, buf, Ow, _ = O.muon_matrix_step(_np(p0[b]), _np(gr[b]), np.zeros(shp, np.float32), lr=0.02,
@@ -425,3 +472,76 @@ def test_sharded_step_from_host_equals_copy_then_step(cuda):
         out.append(params.cpu())
     assert torch.equal(out[0], out[1])
 
+
+
+def _unfused_muon(p, g, buf, lr_eff, decay, steps=5):
+    """momentum, Newton-Schulz and update as three C-ABI calls (the unfused sequence)."""
+    lib = _lib.load()
+    code = 1 if p.dtype == torch.bfloat16 else 0
+    count, rows, cols = p.shape
+    u = torch.empty_like(p)
+    st = _lib.stream_ptr(p.device)
+    _lib.check(lib.po_muon_momentum(g.data_ptr(), buf.data_ptr(), u.data_ptr(), code, u.numel(), 0.95, 1, st), "mom")
+    nbytes = lib.po_ns_workspace_bytes(count, rows, cols)
+    ws = _lib.workspace(nbytes, p.device)
+    _lib.check(lib.po_newton_schulz(u.data_ptr(), code, count, rows, cols, cols, rows * cols, u.data_ptr(), cols,
+                                    rows * cols, steps, 3.4445, -4.7750, 2.0315, 1e-7, -1, ws.data_ptr(), nbytes, st),
+               "ns")
+    sq = torch.zeros(1, dtype=torch.float64, device=p.device)
+    _lib.check(lib.po_muon_apply(p.data_ptr(), u.data_ptr(), code, p.numel(), lr_eff, decay, sq.data_ptr(), st), "app")
+    return u, sq
+
+
+def _fused_muon(p, g, buf, lr_eff, decay, steps=5):
+    lib = _lib.load()
+    code = 1 if p.dtype == torch.bfloat16 else 0
+    count, rows, cols = p.shape
+    o = torch.empty_like(p)
+    sq = torch.zeros(1, dtype=torch.float64, device=p.device)
+    nbytes = lib.po_muon_step_workspace_bytes(count, rows, cols, code)
+    ws = _lib.workspace(nbytes, p.device)
+    _lib.check(lib.po_muon_step(g.data_ptr(), buf.data_ptr(), p.data_ptr(), code, count, rows, cols, 0.95, 1, steps,
+                                3.4445, -4.7750, 2.0315, 1e-7, lr_eff, decay, sq.data_ptr(), o.data_ptr(),
+                                ws.data_ptr(), nbytes, _lib.stream_ptr(p.device)), "po_muon_step")
+    return o, sq
+
+
+@pytest.mark.parametrize("shape,dt,steps", [
+    ((3, 512, 1280), torch.bfloat16, 5),    # direct step 0 from u, wide
+    ((2, 1280, 512), torch.bfloat16, 5),    # direct, tall (transposed operand and addend reads)
+    ((2, 300, 522), torch.bfloat16, 5),     # row pitch not 16-byte aligned: packed step 0
+    ((2, 96, 200), torch.bfloat16, 5),      # small m: split-bf16 schedule
+    ((2, 384, 640), torch.float32, 5),      # fp32 parameters
+    ((2, 512, 768), torch.bfloat16, 1),     # one step: the first update is also the last
+    ((1, 64, 96), torch.bfloat16, 0),       # no step: O is the normalised u
+])
+def test_fused_muon_step_vs_unfused(cuda, shape, dt, steps):
+    """po_muon_step against momentum + Newton-Schulz + update as separate calls:
+    momentum bit-exact; O within the Newton-Schulz tolerance (step 0 reads u
+    unrounded-by-scaling, the unfused path packs a rounded copy of u/||u||);
+    the parameter update bit-exact given the fused call's own O (the
+    reference's in-place op sequence, muon.py:87-91); sum(O^2) consistent."""
+    g = torch.Generator().manual_seed(sum(shape) + steps)
+    p0 = (torch.randn(*shape, generator=g) * 0.02).to(dt)
+    gr = (torch.randn(*shape, generator=g) * 0.02).to(dt)
+    b0 = (torch.randn(*shape, generator=g) * 0.02).to(dt)
+    lr_eff, decay = 0.02 * max(1.0, shape[1] / shape[2]) ** 0.5, 1.0 - 0.02 * 0.01
+    pu, bu = p0.to(cuda), b0.to(cuda)
+    pf, bf = p0.to(cuda), b0.to(cuda)
+    Ou, squ = _unfused_muon(pu, gr.to(cuda), bu, lr_eff, decay, steps)
+    Of, sqf = _fused_muon(pf, gr.to(cuda), bf, lr_eff, decay, steps)
+    assert torch.equal(bu, bf)
+    assert _rel(_np(Of), _np(Ou)) <= NS_TOL
+    p1 = _np(p0) * np.float32(decay)
+    if dt == torch.bfloat16:
+        p1 = O.bf16_round(p1)
+        alpha = O.bf16_round(np.float32(-lr_eff))
+        want_p = O.bf16_round(p1 + alpha * _np(Of))
+    else:
+        want_p = p1 + np.float32(-lr_eff) * _np(Of)
+    if dt == torch.bfloat16:  # alpha and O are bf16: alpha * O is exact in fp32, one rounding as in the kernel
+        np.testing.assert_array_equal(_np(pf), want_p)
+    else:
+        np.testing.assert_allclose(_np(pf), want_p, rtol=1e-6, atol=1e-9)
+    sq_want = float((Of.double() ** 2).sum())
+    assert abs(float(sqf) - sq_want) <= 1e-5 * sq_want

@@ -185,3 +185,27 @@ def test_kfac_band_bounds_balance_the_triangle():
                 assert max(work) <= 1.05 * sum(work) / world
                 assert sum(work) <= d * d  # never more than the full square
 
+
+
+def test_exchange_chunks_end_with_the_cheapest_exchange():
+    """Exchange chunks have decreasing FLOP shares, and within every rank the
+    matrices are ordered by decreasing exchanged bytes per FLOP, so the last
+    chunk (whose all-gather cannot overlap compute) is small and holds the
+    matrices that are cheapest to exchange (Llama: q/o at N = 8)."""
+    from pytorch_opt_b200.dist import ShardLayout, bytes_per_flop, chunk_shares, ns_flops
+    shares = chunk_shares(4)
+    assert abs(sum(shares) - 1.0) < 1e-12 and all(a > b for a, b in zip(shares, shares[1:]))
+    layer = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096), (14336, 4096), (4096, 14336)]
+    for world in (2, 4, 8):
+        lay = ShardLayout(layer * 32, world)
+        seen = set()
+        for r in range(world):
+            per_chunk_flops = [0.0] * lay.chunks
+            worst_bpf = [0.0] * lay.chunks
+            for g in lay.groups[r]:
+                per_chunk_flops[g.chunk] += ns_flops(*g.shape) * len(g.indices)
+                worst_bpf[g.chunk] = max(worst_bpf[g.chunk], bytes_per_flop(*g.shape))
+                seen.update(g.indices)
+            assert per_chunk_flops[-1] <= 0.15 * sum(per_chunk_flops)
+            assert worst_bpf[-1] <= min(w for w in worst_bpf if w > 0)  # the last chunk is cheapest to exchange
+        assert seen == set(range(len(layer) * 32))
