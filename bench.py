@@ -57,10 +57,11 @@ def profiled_traffic(summary: str):
 
     The summary carries one line ``bench-traffic: <bytes> bytes; source
     <fingerprint>``: ncu's dram__bytes_read.sum + dram__bytes_write.sum of the
-    workload's product launches, and the library source fingerprint of the
-    build that was profiled. Returns (bytes or None, profiled fingerprint,
+    workload's product launches, and the fingerprint of the Newton-Schulz
+    path's sources (``build.NS_PATH_SOURCES``) in the build that was profiled. Returns (bytes or None, profiled fingerprint,
     whether it equals the current tree's)."""
-    from pytorch_opt_b200.build import source_fingerprint
+    from pytorch_opt_b200.build import NS_PATH_SOURCES, source_fingerprint
+    current = source_fingerprint(only=NS_PATH_SOURCES)
     try:
         with open(os.path.join(PROFILES, summary)) as f:
             for line in f:
@@ -68,7 +69,7 @@ def profiled_traffic(summary: str):
                     parts = line.split()
                     nbytes = int(parts[1])
                     fp = parts[parts.index("source") + 1] if "source" in parts else None
-                    return nbytes, fp, fp == source_fingerprint()
+                    return nbytes, fp, fp == current
     except (OSError, ValueError, IndexError):
         pass
     return None, None, False

@@ -59,13 +59,26 @@ def _fingerprint(flags: list[str]) -> str:
     return h.hexdigest()
 
 
-def source_fingerprint(debug: bool = False) -> str:
-    """Short hash of every source, header and compiler flag of the library
-    (what a build of the current tree contains); profile summaries record it
-    so a figure taken from them can be matched to the build it describes."""
+# Sources compiled into the Newton-Schulz / Muon step (the benchmark's
+# kernels): the product kernels, their launchers, the NS and Muon drivers and
+# the elementwise passes.
+NS_PATH_SOURCES = ("gemm.cuh", "gemm_pair.cuh", "gemm.cu", "gemm_launch.cuh", "gemm_pair_launch.cuh",
+                   "gemm_host.cuh", "gemm_inst_", "ptx.cuh", "common.cuh", "ns.cu", "muon.cu", "elementwise.cu",
+                   "elementwise.cuh")
+
+
+def source_fingerprint(debug: bool = False, only=None) -> str:
+    """Short hash of the library's sources, headers and compiler flags (what a
+    build of the current tree contains); with ``only`` (file-name prefixes),
+    of those csrc files alone. Profile summaries record the fingerprint of the
+    kernels they profiled, so a figure taken from them can be matched to the
+    build it describes."""
     flags = ARCH_FLAGS + COMMON_FLAGS + (["-DPO_DEBUG=1"] if debug else [])
     h = hashlib.sha256()
-    for p in _sources() + _headers():
+    files = _sources() + _headers()
+    if only is not None:
+        files = [p for p in files if os.path.dirname(p) == CSRC and os.path.basename(p).startswith(tuple(only))]
+    for p in files:
         with open(p, "rb") as f:
             h.update(os.path.relpath(p, REPO_DIR).encode())
             h.update(f.read())
