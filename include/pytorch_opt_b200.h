@@ -179,6 +179,13 @@ int po_precond_apply(const void* L, long long l_ld, const void* G, long long g_l
 int po_precond_apply_norm(const void* L, long long l_ld, const void* G, long long g_ld, const void* R,
                           long long r_ld, void* out, long long out_ld, int dtype, long long m, long long n,
                           double* sq_sum, void* workspace, size_t workspace_bytes, void* stream);
+/* out = op(L) @ G @ op(R), op = transpose when trans_l / trans_r (read in
+ * place, no transposed copy): SOAP's rotations into and out of the factors'
+ * eigenbases, Q_L^T X Q_R and Q_L X Q_R^T (pytorch_opt/optim/soap.py:118-121
+ * with _soap_update :47-64). sq_sum nullable as above. Same workspace. */
+int po_precond_apply_ex(const void* L, long long l_ld, int trans_l, const void* G, long long g_ld, const void* R,
+                        long long r_ld, int trans_r, void* out, long long out_ld, int dtype, long long m, long long n,
+                        double* sq_sum, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
  * EKFAC preconditioning of one layer's gradient V (m x n, fp32): replaces

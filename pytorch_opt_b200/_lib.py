@@ -41,6 +41,7 @@ SIGNATURES = {
     "po_precond_workspace_bytes": (_sz, [_ll, _ll, _i]),
     "po_precond_apply": (_i, [_vp, _ll, _vp, _ll, _vp, _ll, _vp, _ll, _i, _ll, _ll, _vp, _sz, _vp]),
     "po_precond_apply_norm": (_i, [_vp, _ll, _vp, _ll, _vp, _ll, _vp, _ll, _i, _ll, _ll, _vp, _vp, _sz, _vp]),
+    "po_precond_apply_ex": (_i, [_vp, _ll, _i, _vp, _ll, _vp, _ll, _i, _vp, _ll, _i, _ll, _ll, _vp, _vp, _sz, _vp]),
     "po_ekfac_workspace_bytes": (_sz, [_ll, _ll]),
     "po_ekfac_precondition": (_i, [_vp, _ll, _vp, _ll, _vp, _ll, _vp, _ll, _vp, _ll, _ll, _ll, _i, _f, _f, _vp, _sz,
                                    _vp]),

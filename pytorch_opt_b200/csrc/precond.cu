@@ -66,16 +66,16 @@ extern "C" size_t po_precond_workspace_bytes(long long m, long long n, int dtype
   return ar.used + 256;
 }
 
-extern "C" int po_precond_apply_norm(const void* L, long long l_ld, const void* G, long long g_ld, const void* R,
-                                     long long r_ld, void* out, long long out_ld, int dtype, long long m,
-                                     long long n, double* sq_sum, void* workspace, size_t workspace_bytes,
-                                     void* stream);
+extern "C" int po_precond_apply_ex(const void* L, long long l_ld, int trans_l, const void* G, long long g_ld,
+                                   const void* R, long long r_ld, int trans_r, void* out, long long out_ld, int dtype,
+                                   long long m, long long n, double* sq_sum, void* workspace, size_t workspace_bytes,
+                                   void* stream);
 
 extern "C" int po_precond_apply(const void* L, long long l_ld, const void* G, long long g_ld, const void* R,
                                 long long r_ld, void* out, long long out_ld, int dtype, long long m, long long n,
                                 void* workspace, size_t workspace_bytes, void* stream) {
-  return po_precond_apply_norm(L, l_ld, G, g_ld, R, r_ld, out, out_ld, dtype, m, n, nullptr, workspace,
-                               workspace_bytes, stream);
+  return po_precond_apply_ex(L, l_ld, 0, G, g_ld, R, r_ld, 0, out, out_ld, dtype, m, n, nullptr, workspace,
+                             workspace_bytes, stream);
 }
 
 // As po_precond_apply; with sq_sum (device fp64) also ||out||_F^2 summed by
@@ -84,6 +84,16 @@ extern "C" int po_precond_apply_norm(const void* L, long long l_ld, const void* 
                                      long long r_ld, void* out, long long out_ld, int dtype, long long m,
                                      long long n, double* sq_sum, void* workspace, size_t workspace_bytes,
                                      void* stream) {
+  return po_precond_apply_ex(L, l_ld, 0, G, g_ld, R, r_ld, 0, out, out_ld, dtype, m, n, sq_sum, workspace,
+                             workspace_bytes, stream);
+}
+
+// out = op(L) G op(R) with op = transpose when trans_l / trans_r: the staged
+// operand is read MN-major instead of K-major, so no transposed copy is made.
+extern "C" int po_precond_apply_ex(const void* L, long long l_ld, int trans_l, const void* G, long long g_ld,
+                                   const void* R, long long r_ld, int trans_r, void* out, long long out_ld, int dtype,
+                                   long long m, long long n, double* sq_sum, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
   if (dtype != PO_F32 && dtype != PO_BF16) return set_error(PO_ERR_ARG, "precond_apply: dtype must be fp32 or bf16");
   if (m < 0 || n < 0) return set_error(PO_ERR_ARG, "precond_apply: negative size");
   if (sq_sum != nullptr) {
@@ -123,6 +133,7 @@ extern "C" int po_precond_apply_norm(const void* L, long long l_ld, const void* 
     g1.b[1] = oview(B.gl, split, m, n, B.ldg);
     g1.npass = 3;
   }
+  g1.a_kmajor = !trans_l;  // L [m][m] read K-major is L, MN-major is L^T
   g1.b_kmajor = false;
   g1.sched = B.sched;
   g1.chunked = split && 3 * m > 1024;
@@ -145,7 +156,7 @@ extern "C" int po_precond_apply_norm(const void* L, long long l_ld, const void* 
     g2.b[1] = oview(B.rl, split, n, n, B.ldr);
     g2.npass = 3;
   }
-  g2.b_kmajor = false;
+  g2.b_kmajor = trans_r != 0;  // R [n][n] read as [K][N] is R, as [N][K] is R^T
   g2.sched = B.sched;
   g2.chunked = split && 3 * n > 1024;
   g2.epi.alpha = 1.0f;

@@ -22,6 +22,10 @@ make in the reference's sources to use the B200 kernels:
   condition number; ``KFAC._precondition`` (:140-147) runs ``iG @ V @ iA`` on
   the two-sided apply kernel and ``EKFAC._precondition`` (``optim/ekfac.py:44-58``)
   on the rotated-diagonal kernel.
+* SOAP: ``SOAP._soap_update`` (``optim/soap.py:47-64``) receives its
+  rotations into and out of the factors' eigenbases as the two-sided apply
+  kernel with transposed operands read in place (``soap.py:118-121``); the
+  eigenbases themselves stay the reference's fp64 ``eigh`` (``:98-110``).
 
 Every replacement falls through to the reference's original code for inputs
 this library does not serve (CPU tensors, fp64 factors), exactly as the
@@ -192,9 +196,21 @@ def _install_kfac(pytorch_opt) -> None:
                                                             self._scale_decay, self.param_groups[0]["damping"])
         return out.to(V.dtype)
 
+    soap_mod = importlib.import_module(pytorch_opt.__name__ + ".optim.soap")
+    SOAP = soap_mod.SOAP
+    orig_soap_update = SOAP.__dict__["_soap_update"]
+
+    def _soap_update(p, g, st, group, *, transform, back):
+        QL, QR = st.get("Q_L"), st.get("Q_R")
+        if QL is not None and _on_gpu(QL, QR, g) and QL.dtype == torch.float32 and g.dtype == torch.float32:
+            transform = lambda x: native.rotate_two_sided(QL, x, QR, trans_l=True)  # noqa: E731  QL^T x QR
+            back = lambda x: native.rotate_two_sided(QL, x, QR, trans_r=True)  # noqa: E731  QL x QR^T
+        return orig_soap_update.__func__(p, g, st, group, transform=transform, back=back)
+
     _SAVED["kfac"] = [(KronTracker, "_on_grad_out", orig_on_grad), (kfac_mod, "kfac_factored_damping", orig_damping),
                       (KFAC, "_damped_inverse", orig_inverse), (KFAC, "_precondition", orig_precond),
-                      (EKFAC, "_precondition", orig_eprecond)]
+                      (EKFAC, "_precondition", orig_eprecond), (SOAP, "_soap_update", orig_soap_update)]
+    SOAP._soap_update = staticmethod(_soap_update)
     KronTracker._on_grad_out = _on_grad_out
     kfac_mod.kfac_factored_damping = kfac_factored_damping
     KFAC._damped_inverse = staticmethod(_damped_inverse)

@@ -152,7 +152,16 @@ def precond_apply_two_sided(L_root: torch.Tensor, G: torch.Tensor, R_root: torch
     return _precond(L_root, G, R_root, False)[0]
 
 
-def _precond(L_root, G, R_root, want_norm: bool):
+def rotate_two_sided(QL: torch.Tensor, G: torch.Tensor, QR: torch.Tensor, trans_l: bool = False,
+                     trans_r: bool = False) -> torch.Tensor:
+    """op(QL) @ G @ op(QR), op = transpose when requested, without transposed
+    copies: SOAP's rotations into the factors' eigenbases, ``QL^T G QR``
+    (``trans_l``), and back, ``QL G QR^T`` (``trans_r``)
+    (``pytorch_opt/optim/soap.py:118-121``)."""
+    return _precond(QL, G, QR, False, trans_l, trans_r)[0]
+
+
+def _precond(L_root, G, R_root, want_norm: bool, trans_l: bool = False, trans_r: bool = False):
     dev = _require_cuda(L_root, G, R_root)
     if G.dim() != 2 or L_root.dim() != 2 or R_root.dim() != 2:
         raise RuntimeError("precond_apply_two_sided expects 2D operands")
@@ -169,12 +178,9 @@ def _precond(L_root, G, R_root, want_norm: bool):
             code = _lib.DTYPE_CODE[dt]
             nbytes = lib.po_precond_workspace_bytes(m, n, code)
             ws = _lib.workspace(nbytes, dev)
-            if want_norm:
-                _call("po_precond_apply_norm", Lc.data_ptr(), m, Gc.data_ptr(), n, Rc.data_ptr(), n, out.data_ptr(),
-                      n, code, m, n, sq.data_ptr(), ws.data_ptr(), nbytes, _lib.stream_ptr(dev))
-            else:
-                _call("po_precond_apply", Lc.data_ptr(), m, Gc.data_ptr(), n, Rc.data_ptr(), n, out.data_ptr(), n,
-                      code, m, n, ws.data_ptr(), nbytes, _lib.stream_ptr(dev))
+            _call("po_precond_apply_ex", Lc.data_ptr(), m, 1 if trans_l else 0, Gc.data_ptr(), n, Rc.data_ptr(), n,
+                  1 if trans_r else 0, out.data_ptr(), n, code, m, n, sq.data_ptr() if want_norm else None,
+                  ws.data_ptr(), nbytes, _lib.stream_ptr(dev))
     return (out if out.dtype == G.dtype else out.to(G.dtype)), sq
 
 

@@ -56,7 +56,9 @@ def test_cpu_tensors_keep_the_reference_path(po):
     from pytorch_opt import ops
     from pytorch_opt.optim import kfac as kfac_mod
     before = {k: getattr(ops, k) for k in ("_NATIVE", "newton_schulz_orthogonalize", "inverse_matrix_root")}
-    k_before = (kfac_mod.kfac_factored_damping, kfac_mod.KFAC.__dict__["_damped_inverse"])
+    from pytorch_opt.optim import soap as soap_mod
+    k_before = (kfac_mod.kfac_factored_damping, kfac_mod.KFAC.__dict__["_damped_inverse"],
+                soap_mod.SOAP.__dict__["_soap_update"])
     muon_ref = _muon_params(po)
     kfac_ref, cond_ref = _kfac_params(po)
     dropin.install(po)
@@ -76,4 +78,5 @@ def test_cpu_tensors_keep_the_reference_path(po):
         dropin.uninstall()
     for k, v in before.items():
         assert getattr(ops, k) is v
-    assert (kfac_mod.kfac_factored_damping, kfac_mod.KFAC.__dict__["_damped_inverse"]) == k_before
+    assert (kfac_mod.kfac_factored_damping, kfac_mod.KFAC.__dict__["_damped_inverse"],
+            soap_mod.SOAP.__dict__["_soap_update"]) == k_before

@@ -160,29 +160,37 @@ def test_shampoo_dropin(po, cuda, root_method):
 
 
 def test_soap_dropin(po, cuda):
-    """SOAP's ops call (``optim/soap.py:95``) is the Kronecker factor update;
-    its factors after three steps are compared with the reference's. The
-    parameter change itself is not comparable element by element: SOAP's
-    first Adam steps in the eigenbasis normalise rotated gradient entries
-    that are zero up to rounding to +-1, so even an exactly rounded fp32
-    product (the reference's own CPU product differs from it in the last
-    bit) moves the 3-step update of these shapes by ~0.4 relative. Its
-    magnitude is the same: compared to 5 %."""
+    """SOAP's ops call (``optim/soap.py:95``) is the Kronecker factor update,
+    and its rotations into and out of the eigenbases run on the two-sided
+    apply kernel (``_soap_update``). Its factors after three steps are
+    compared with the reference's. The parameter change is compared with
+    eps = 1e-3: with the default eps (1e-8) SOAP's first Adam steps in the
+    eigenbasis normalise rotated entries that are zero up to rounding to +-1
+    (at step 1 the rotated gradient is diagonal), so even an exactly rounded
+    fp32 product moves the default-eps update by ~0.4; with eps = 1e-3 those
+    entries stay negligible and the update is well defined."""
     from pytorch_opt.optim import SOAP
-    kw = dict(lr=3e-3, precondition_frequency=1)
     shapes = [(64, 48), (40, 72), (200, 160)]
-    ref, opt_r = _matrix_run(SOAP, shapes, 3, 3, "cpu", **kw)
-    got, opt_g = _matrix_run(SOAP, shapes, 3, 3, cuda, **kw)
+    calls = []
+    orig = native.rotate_two_sided
+    native.rotate_two_sided = lambda *a, **k: calls.append(1) or orig(*a, **k)
+    try:
+        _, opt_r = _matrix_run(SOAP, shapes, 3, 3, "cpu", lr=3e-3, precondition_frequency=1)
+        _, opt_g = _matrix_run(SOAP, shapes, 3, 3, cuda, lr=3e-3, precondition_frequency=1)
+        ref, _ = _matrix_run(SOAP, shapes, 3, 3, "cpu", lr=3e-3, precondition_frequency=1, eps=1e-3)
+        got, _ = _matrix_run(SOAP, shapes, 3, 3, cuda, lr=3e-3, precondition_frequency=1, eps=1e-3)
+    finally:
+        native.rotate_two_sided = orig
+    assert len(calls) == 2 * 3 * len(shapes) * 3  # transform(g), transform(m), back(update) per matrix, step, run
     ferr = []
     for pg, pr in zip(opt_g.param_groups[0]["params"], opt_r.param_groups[0]["params"]):
         sg, sr = opt_g.state[pg], opt_r.state[pr]
         ferr += [_rel(sg["L"], sr["L"]), _rel(sg["R"], sr["R"])]
-    norms = [float(a.norm() / b.norm()) for a, b in zip(got, ref)]
-    print(f"SOAP drop-in: factor rel errors {[f'{e:.1e}' for e in ferr]}, update norm ratios "
-          f"{[f'{x:.4f}' for x in norms]}")
+    errs = [_rel(a, b) for a, b in zip(got, ref)]
+    print(f"SOAP drop-in: factor rel errors {[f'{e:.1e}' for e in ferr]}; eps=1e-3 parameter-change rel errors "
+          f"{[f'{e:.2e}' for e in errs]}")
     assert max(ferr) <= 1e-5
-    assert all(torch.isfinite(d).all() for d in got)
-    assert all(abs(x - 1.0) <= 0.05 for x in norms)
+    assert max(errs) <= 1e-3
 
 
 def _mlp():

@@ -350,6 +350,20 @@ def test_precond_golden_and_oracle(cuda):
     assert _rel(_np(got), O.precond_apply(_np(L).astype(np.float64), _np(G), _np(R))) <= FACTOR_TOL
 
 
+@pytest.mark.parametrize("trans_l,trans_r", [(True, False), (False, True), (True, True)])
+def test_rotate_two_sided_transposes_in_place(cuda, trans_l, trans_r):
+    """op(QL) G op(QR) with transposed operands read in place (SOAP's rotations
+    QL^T G QR and QL G QR^T), split-tf32: fp32-grade against fp64."""
+    g = torch.Generator().manual_seed(17)
+    m, n = 300, 520
+    QL = torch.linalg.qr(torch.randn(m, m, generator=g, dtype=torch.float64))[0]
+    QR = torch.linalg.qr(torch.randn(n, n, generator=g, dtype=torch.float64))[0]
+    G = torch.randn(m, n, generator=g, dtype=torch.float64)
+    got = native.rotate_two_sided(QL.float().to(cuda), G.float().to(cuda), QR.float().to(cuda), trans_l, trans_r)
+    want = (QL.T if trans_l else QL) @ G @ (QR.T if trans_r else QR)
+    assert _rel(_np(got), want.numpy()) <= 1e-5
+
+
 @pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
 def test_precond_grafted_norm_from_epilogue(cuda, dt):
     """Grafting (shampoo.py:128-137): the epilogue's ||P||^2 matches the norm of
