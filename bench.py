@@ -805,9 +805,10 @@ def run_secondary(args, rank):
 
 
 def run_kfac_split(args, rank, world, local_rank):
-    """KFAC A and G factor updates (config 4 shapes) shared by all ranks: row bands + all_reduce."""
+    """KFAC A and G factor updates (config 4 shapes) shared by all ranks: row bands of each factor
+    (``--kfac-split bands``) or whole factors per rank (``--kfac-split factors``)."""
     import torch.distributed as dist
-    from pytorch_opt_b200.dist import sharded_syrk_ema_
+    from pytorch_opt_b200.dist import sharded_factor_updates_, sharded_syrk_ema_
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     if world > 1:
@@ -821,8 +822,11 @@ def run_kfac_split(args, rank, world, local_rank):
     n = 8192
 
     def update(first=False):
-        sharded_syrk_ema_(A, a, 1.0 / n, 0.95, first, rank, world)
-        sharded_syrk_ema_(Gf, gr, float(n), 0.95, first, rank, world)
+        if args.kfac_split == "factors":
+            sharded_factor_updates_([(A, a, 1.0 / n, 0.95, first), (Gf, gr, float(n), 0.95, first)], rank, world)
+        else:
+            sharded_syrk_ema_(A, a, 1.0 / n, 0.95, first, rank, world)
+            sharded_syrk_ema_(Gf, gr, float(n), 0.95, first, rank, world)
     update(True)
     for _ in range(args.warmup):
         update()
@@ -852,11 +856,15 @@ def run_kfac_split(args, rank, world, local_rank):
         pk = peaks()
         tf = fl / (ms * 1e-3) / 1e12
         print(json.dumps({
-            "metric": "KFAC factor update ms (A and G, 8192x4096 -> 4096^2), split by row bands", "value": round(ms, 4),
+            "metric": f"KFAC factor update ms (A and G, 8192x4096 -> 4096^2), split by {args.kfac_split}",
+            "value": round(ms, 4),
             "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "KFAC SYRK+EMA of A and G shared by all ranks: row bands of equal work, "
-                                   "one all_reduce and a mirror per factor", "parallelism": f"row bands x{world}"},
+            "config": {"workload": "KFAC SYRK+EMA of A and G shared by all ranks: "
+                                   + ("whole factors per rank (LPT) + one broadcast per factor"
+                                      if args.kfac_split == "factors" else
+                                      "row bands of equal work, one all_gather and a mirror per factor"),
+                       "parallelism": f"{args.kfac_split} x{world}"},
             "roofline": {"bound": "tensor", "kernel": "tc_gemm_kernel (chunked)", "achieved": round(tf, 1),
                          "peak": pk["bf16_sustained"], "unit": "TFLOP/s", "frac": round(tf / pk["bf16_sustained"], 3),
                          "traffic": None, "how": "dense SYRK FLOPs of both factors / the slowest rank's time"},
@@ -889,6 +897,8 @@ def main(argv=None) -> int:
     ap.add_argument("--gemm", type=int, nargs=3, default=(8192, 8192, 8192), metavar=("M", "N", "K"),
                     help="shape of --workload gemm")
     ap.add_argument("--gemm-dtype", choices=("bf16", "tf32"), default="bf16")
+    ap.add_argument("--kfac-split", choices=("factors", "bands"), default="factors",
+                    help="--workload kfac_split: whole factors per rank, or row bands of each factor")
     ap.add_argument("--exchange-chunks", type=int, default=None,
                     help="all-gather chunks per step for N > 1 (default 4; 1 = one all-gather after the local step)")
     args = ap.parse_args(argv)

@@ -494,3 +494,35 @@ def sharded_syrk_ema_(F: torch.Tensor, X: torch.Tensor, alpha: float, beta: floa
         if b > a:
             D[a:b, :b] = buf[k, :b - a, :b]
     return mirror_lower_(F, D)
+
+
+def sharded_factor_updates_(updates: list, rank: int = 0, world: int = 1, group=None, compute=None) -> list[int]:
+    """Many KFAC factor updates (``kron.py:95-113``) shared by the ranks one
+    whole factor at a time.
+
+    ``updates``: list of ``(F, X, alpha, beta, first)`` (F d x d fp32, X rows
+    x d), the same list on every rank. The factors are assigned to ranks by
+    greedy LPT over their SYRK work (rows * d^2); each rank runs the fused
+    triangular SYRK+EMA kernel on its own factors, and every factor is then
+    broadcast from its owner (NCCL over NVLink), so all ranks end with every
+    updated factor. Returns the owner of each update. Unlike the row-band
+    split (``sharded_syrk_ema_``), no factor is cut, so each update keeps the
+    fused kernel's efficiency; it needs at least as many factors as ranks to
+    use every GPU (config 4: A and G on two ranks). ``compute(F, X, alpha,
+    beta, first)`` replaces the kernel (host-side tests over gloo).
+    """
+    if compute is None:
+        from . import native
+        compute = native.kron_syrk_ema_
+    costs = [float(X.shape[0]) * F.shape[0] ** 2 for F, X, *_ in updates]
+    owners = [0] * len(updates)
+    for r, items in enumerate(lpt_assign(costs, world)):
+        for i in items:
+            owners[i] = r
+    for i, (F, X, alpha, beta, first) in enumerate(updates):
+        if owners[i] == rank:
+            compute(F, X, alpha, beta, first)
+    if world > 1:
+        for i, (F, *_rest) in enumerate(updates):
+            dist.broadcast(F, src=owners[i], group=group)
+    return owners

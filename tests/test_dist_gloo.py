@@ -85,6 +85,28 @@ def _worker_band_syrk(rank, world, port, q):
         q.put((rank, traceback.format_exc()))
 
 
+def _worker_factor_sharding(rank, world, port, q):
+    try:
+        from pytorch_opt_b200.dist import sharded_factor_updates_
+        _init(rank, world, port)
+        g = torch.Generator().manual_seed(6)
+        Xs = [torch.randn(32, d, generator=g, dtype=torch.float64) for d in (20, 12, 30)]
+        Fs = [torch.full((X.shape[1], X.shape[1]), float("nan"), dtype=torch.float64) for X in Xs]
+
+        def syrk_ema(F, X, alpha, beta, first):  # stands in for the fused kernel
+            S = alpha * X.T @ X
+            F.copy_(S if first else beta * F + (1 - beta) * S)
+
+        owners = sharded_factor_updates_([(F, X, 0.5, 0.9, True) for F, X in zip(Fs, Xs)], rank, world,
+                                         compute=syrk_ema)
+        ok = sorted(set(owners)) == list(range(world))
+        ok = ok and all(torch.allclose(F, 0.5 * X.T @ X) for F, X in zip(Fs, Xs))  # every factor on every rank
+        q.put((rank, bool(ok)))
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, traceback.format_exc()))
+
+
 def _worker_dead_peer(rank, world, port, q):
     try:
         _init(rank, world, port, timeout_s=5)
@@ -136,3 +158,10 @@ def test_band_split_factor_update_two_ranks():
     res = _run(_worker_band_syrk, 2)
     assert res[0][1] is True and res[1][1] is True, res
 
+
+
+def test_factor_sharding_two_ranks():
+    """Whole factors per rank (LPT), each broadcast from its owner: every rank
+    ends with every updated factor, and both ranks own work."""
+    res = _run(_worker_factor_sharding, 2)
+    assert res[0][1] is True and res[1][1] is True, res
