@@ -84,6 +84,51 @@ def bytes_per_flop(rows: int, cols: int) -> float:
     return 2.0 * rows * cols / ns_flops(rows, cols)
 
 
+# Pinned host-to-device copy rate over the fused Muon step's FLOP rate on one
+# B200 (about 50 GB/s against about 1.4 PFLOP/s): a batch whose gradient bytes
+# per NS FLOP exceed this copies longer than it computes.
+H2D_BYTES_PER_FLOP = 50e9 / 1.4e15
+
+
+def host_copy_jobs(chunks: list, max_batch: int = 32,
+                   bytes_per_flop: float = H2D_BYTES_PER_FLOP) -> list[list[tuple[int, int, int]]]:
+    """Order and batch sizes in which gradients copied from host memory are stepped.
+
+    ``chunks``: per exchange chunk, ``(k, count, rows, cols, elem_bytes)`` per
+    shape group. The copies (one stream) and the steps (another) form a
+    two-stage flow shop. Within a chunk the groups follow Johnson's rule:
+    groups whose matrices compute longer than they copy first, by increasing
+    copy time, then the others by decreasing compute time. Each group is cut
+    into batches as an estimate of both streams goes along: a batch is as
+    large as the copy stream's lead over the queued compute lets its copy
+    land before the step stream needs it (at least 1, at most ``max_batch``
+    matrices), so the step opens with one matrix and the batches grow
+    geometrically. Returns ``(k, start, stop)`` triples per chunk.
+    """
+    copy_end = compute_end = 0.0
+    out = []
+    for groups in chunks:
+        per = []
+        for k, count, rows, cols, es in groups:
+            a = float(rows * cols * es)
+            b = ns_flops(rows, cols) * bytes_per_flop
+            per.append((k, count, a, b))
+        order = sorted((g for g in per if g[2] < g[3]), key=lambda g: (g[2], g[0])) + \
+            sorted((g for g in per if g[2] >= g[3]), key=lambda g: (-g[3], g[0]))
+        jobs = []
+        for k, count, a, b in order:
+            start = 0
+            while start < count:
+                n = int((compute_end - copy_end) // a) if compute_end > copy_end else 0
+                n = max(1, min(max_batch, count - start, n))
+                copy_end += n * a
+                compute_end = max(compute_end, copy_end) + n * b
+                jobs.append((k, start, start + n))
+                start += n
+        out.append(jobs)
+    return out
+
+
 class ShardLayout:
     """Placement of matrices in a flat parameter buffer, sharded by rank and chunk.
 
@@ -238,17 +283,21 @@ class ShardedMuon:
         else:
             self.groups = list(zip(pv, gv))
         self._sq = torch.zeros(max(len(self.groups), 1), dtype=torch.float64, device=params_flat.device)
+        self.h2d_bytes_per_flop = H2D_BYTES_PER_FLOP  # batch sizing of step_from_host (host_copy_jobs)
         self._ws = None
         if compute is None and self.groups:
             need = max(ns_workspace_bytes(*g.params.shape, dtype=g.params.dtype) for g in self.groups)
             self._ws = torch.empty(need, dtype=torch.uint8, device=params_flat.device)
 
-    def _step_group(self, k: int, ns_events: list | None) -> None:
+    def _step_group(self, k: int, ns_events: list | None, span: tuple[int, int] | None = None) -> None:
         if self.compute is not None:
             p, g = self.groups[k]
+            if span is not None:
+                p, g = p[span[0]:span[1]], g[span[0]:span[1]]
             self.compute(p, g)
         else:
-            muon_group_step(self.groups[k], sq_sum=self._sq[k], workspace=self._ws, ns_events=ns_events, **self.hp)
+            muon_group_step(self.groups[k], sq_sum=self._sq[k], workspace=self._ws, ns_events=ns_events, span=span,
+                            **self.hp)
 
     def _gather_chunk(self, c: int):
         """Start chunk c's all-gather (NCCL orders it after the work already queued on the current stream)."""
@@ -256,14 +305,18 @@ class ShardedMuon:
                                            self.layout.chunk_part(self.params_flat, self.rank, c),
                                            group=self.pg, async_op=True)
 
-    def _run(self, order_of_chunk, ns_events, before_group=None, tail_events=None) -> None:
+    def _run(self, jobs_of_chunk, ns_events, before_job=None, tail_events=None) -> None:
+        """``jobs_of_chunk(c)``: group indices, or ``(k, start, stop)`` spans of groups, in step order."""
         self._sq.zero_()
         pending = []
         for c in range(self.layout.chunks):
-            for k in order_of_chunk(c):
-                if before_group is not None:
-                    before_group(k)
-                self._step_group(k, ns_events)
+            for job in jobs_of_chunk(c):
+                if before_job is not None:
+                    before_job(job)
+                if isinstance(job, tuple):
+                    self._step_group(job[0], ns_events, span=job[1:])
+                else:
+                    self._step_group(job, ns_events)
             if self.layout.world > 1:
                 pending.append(self._gather_chunk(c))
         if tail_events is not None:  # after the last local kernel, before the wait for the last exchange
@@ -306,32 +359,35 @@ class ShardedMuon:
 
         ``host_slot``: this rank's gradient slot (``layout.slot`` elements of
         the gradient dtype, chunk after chunk as ``ShardLayout.slot_tensor``
-        lays it out), ideally in pinned memory. Each shape group's gradients
-        are copied on a side stream (within a chunk, smallest group first) and
-        the group is stepped as soon as its copy lands, so the copies overlap
-        the Newton–Schulz work of the groups before them; only the first copy
-        is exposed. Results are identical to copying the slot and calling
-        ``step``.
+        lays it out), ideally in pinned memory. The gradients are copied on a
+        side stream in batches (``host_copy_jobs``: Johnson's order within each
+        exchange chunk, batches sized to the copy stream's lead, the first one
+        a single matrix) and each batch is stepped as soon as its copy lands,
+        so the copies overlap the Newton–Schulz work of the batches before
+        them and only the first matrix's copy is exposed. Results are identical to
+        copying the slot and calling ``step``.
         """
         if host_slot.numel() < self.layout.slot:
             raise ValueError(f"host_slot holds {host_slot.numel()} elements, the slot needs {self.layout.slot}")
         groups = self.layout.groups[self.rank]
 
-        def host_view(k):
-            g = groups[k]
-            r, c = g.shape
-            return host_slot[g.offset:g.offset + len(g.indices) * r * c].view(len(g.indices), r, c)
-
         def grad_of(k):
             return self.groups[k][1] if self.compute is not None else self.groups[k].grads
 
-        def order(c):
-            return sorted(self._chunk_groups(c), key=lambda k: (grad_of(k).numel(), k))
+        def host_view(k, s, e):
+            g = groups[k]
+            r, c = g.shape
+            return host_slot[g.offset + s * r * c:g.offset + e * r * c].view(e - s, r, c)
 
+        es = host_slot.element_size()
+        jobs = dict(enumerate(host_copy_jobs(
+            [[(k, len(groups[k].indices), *groups[k].shape, es) for k in self._chunk_groups(c)]
+             for c in range(self.layout.chunks)], bytes_per_flop=self.h2d_bytes_per_flop)))
         if self.compute is not None:  # host-side (gloo) path: no streams
-            for k in range(len(self.groups)):
-                grad_of(k).copy_(host_view(k))
-            self._run(order, ns_events)
+            for c in range(self.layout.chunks):
+                for k, s, e in jobs[c]:
+                    grad_of(k)[s:e].copy_(host_view(k, s, e))
+            self._run(jobs.__getitem__, ns_events)
             return
         dev = self.params_flat.device
         main = torch.cuda.current_stream(dev)
@@ -342,12 +398,13 @@ class ShardedMuon:
         landed = {}
         with torch.cuda.stream(cs):
             for c in range(self.layout.chunks):
-                for k in order(c):
-                    grad_of(k).copy_(host_view(k), non_blocking=True)
+                for job in jobs[c]:
+                    k, s, e = job
+                    grad_of(k)[s:e].copy_(host_view(k, s, e), non_blocking=True)
                     ev = torch.cuda.Event()
                     ev.record(cs)
-                    landed[k] = ev
-        self._run(order, ns_events, before_group=lambda k: main.wait_event(landed[k]))
+                    landed[job] = ev
+        self._run(jobs.__getitem__, ns_events, before_job=lambda job: main.wait_event(landed[job]))
 
     def launches_per_step(self) -> int:
         """Kernels this library launches per local step (the all-gather is NCCL's)."""

@@ -70,7 +70,8 @@ def ns_workspace_bytes(count: int, rows: int, cols: int, max_batch: int = 32, dt
 def muon_group_step(group: MuonGroup, lr: float = 0.02, momentum: float = 0.95, nesterov: bool = True,
                     ns_steps: int = 5, weight_decay: float = 0.0, lr_adjust: str = "spectral",
                     sq_sum: torch.Tensor | None = None, coeffs=(3.4445, -4.7750, 2.0315), eps: float = 1e-7,
-                    workspace: torch.Tensor | None = None, max_batch: int = 32, ns_events: list | None = None) -> None:
+                    workspace: torch.Tensor | None = None, max_batch: int = 32, ns_events: list | None = None,
+                    span: tuple[int, int] | None = None) -> None:
     """One Muon update of every matrix in ``group`` (in place).
 
     ``sq_sum``: optional fp64 CUDA scalar; receives ``sum(O^2)`` of the
@@ -80,6 +81,8 @@ def muon_group_step(group: MuonGroup, lr: float = 0.02, momentum: float = 0.95, 
     stream); the fused step runs on at most ``max_batch`` matrices per call to
     bound it. ``ns_events``: optional list; a (start, end) pair of CUDA events
     recorded around the group's fused steps is appended (for timing).
+    ``span``: optional ``(start, stop)``; only matrices ``start..stop-1`` of
+    the group are updated (their results do not depend on the split).
     """
     lib = _lib.load()
     p = group.params
@@ -108,6 +111,11 @@ def muon_group_step(group: MuonGroup, lr: float = 0.02, momentum: float = 0.95, 
     # Measurement switch: PO_MUON_FUSED=0 runs the unfused calls (momentum,
     # Newton-Schulz on a packed copy, update) for A/B timing of the fused step.
     unfused = os.environ.get("PO_MUON_FUSED", "1") == "0"
+    first, stop = (0, count) if span is None else (int(span[0]), int(span[1]))
+    if not 0 <= first <= stop <= count:
+        raise ValueError(f"span {span} outside the group's {count} matrices")
+    if unfused and (first, stop) != (0, count):
+        raise ValueError("PO_MUON_FUSED=0 steps whole groups only")
     with torch.cuda.device(dev):
         if ns_events is not None:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -115,8 +123,8 @@ def muon_group_step(group: MuonGroup, lr: float = 0.02, momentum: float = 0.95, 
         if unfused:
             _unfused_group_step(lib, group, code, stream, workspace, momentum, nesterov, ns_steps, coeffs, eps, eff,
                                 decay, sq_ptr, max_batch)
-        for start in range(0, count if not unfused else 0, max_batch):
-            k = min(max_batch, count - start)
+        for start in range(first, stop if not unfused else first, max_batch):
+            k = min(max_batch, stop - start)
             off = start * mat * es
             o_ptr = group._u.data_ptr() + off if group.keep_update else None
             _lib.check(lib.po_muon_step(group.grads.data_ptr() + off, group.momentum.data_ptr() + off,

@@ -463,11 +463,14 @@ def test_grouped_muon_vs_oracle_gpt2_shapes(cuda):
 
 
 def test_sharded_step_from_host_equals_copy_then_step(cuda):
-    """Per-group host-to-device copies overlapped with the step give the same
-    parameters, bit for bit, as one slot copy followed by the step."""
-    from pytorch_opt_b200.dist import ShardLayout, ShardedMuon
-    shapes = [(768, 2304), (768, 768), (3072, 768), (768, 768), (256, 1024)]
+    """Host-to-device copies in batches (parts of groups) overlapped with the
+    step give the same parameters, bit for bit, as one slot copy followed by
+    the step."""
+    from pytorch_opt_b200.dist import ShardLayout, ShardedMuon, host_copy_jobs
+    shapes = [(768, 2304), (768, 768), (3072, 768), (768, 768), (256, 1024)] + [(2048, 2048)] * 9
     lay = ShardLayout(shapes, 1)
+    jobs = host_copy_jobs([[(k, len(gr.indices), *gr.shape, 2) for k, gr in enumerate(lay.groups[0])]])[0]
+    assert any(0 < s or e < len(lay.groups[0][k].indices) for k, s, e in jobs)  # some groups are split
     g = torch.Generator().manual_seed(9)
     p0 = (torch.randn(lay.numel, generator=g) * 0.02).bfloat16()
     host = (torch.randn(lay.slot, generator=g) * 0.02).bfloat16().pin_memory()

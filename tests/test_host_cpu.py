@@ -172,6 +172,39 @@ def test_step_from_host_matches_copy_then_step_on_cpu():
             host[:-1])
 
 
+def test_host_copy_jobs_expose_only_the_first_matrix_copy():
+    """Host-gradient batches (Johnson's order, sized to the copy stream's
+    lead) cover every matrix once, and in a copy-then-compute flow shop with
+    the Llama-3-8B groups only the first (one-matrix) copy is left without
+    compute to hide it."""
+    from pytorch_opt_b200.dist import H2D_BYTES_PER_FLOP, host_copy_jobs, ns_flops
+    groups = [(0, 64, 4096, 4096, 2), (1, 64, 1024, 4096, 2), (2, 64, 14336, 4096, 2), (3, 32, 4096, 14336, 2)]
+    for split in ([groups], [groups[:2], groups[2:]]):
+        jobs = [j for c in host_copy_jobs(split) for j in c]
+        seen = {k: [] for k, *_ in groups}
+        for k, s, e in jobs:
+            assert 0 < e - s <= 32
+            seen[k].extend(range(s, e))
+        assert all(sorted(v) == list(range(groups[k][1])) for k, v in seen.items())
+        assert jobs[0][2] - jobs[0][1] == 1
+        shape = {k: (r, c, es) for k, _, r, c, es in groups}
+        copy_end = compute_end = busy = 0.0
+        for i, (k, s, e) in enumerate(jobs):
+            r, c, es = shape[k]
+            a = (e - s) * r * c * es
+            b = (e - s) * ns_flops(r, c) * H2D_BYTES_PER_FLOP
+            copy_end += a
+            compute_end = max(compute_end, copy_end) + b
+            busy += b
+            if i == 0:
+                first_copy = a
+        assert compute_end - busy <= first_copy * (1 + 1e-9)
+    jobs = host_copy_jobs([groups])[0]
+    assert len(jobs) <= 16
+    kinds = [shape[k][0] == 1024 for k, _, _ in jobs]  # copy-bound batches (k/v) come last
+    assert kinds == sorted(kinds)
+
+
 def test_kfac_band_bounds_balance_the_triangle():
     from pytorch_opt_b200.dist import kfac_band_bounds
     for d in (4096, 1000, 300):
