@@ -359,6 +359,8 @@ def run_ours(args, rank, world, local_rank):
     gemm_tflops = min(all_ranks(local_flops / (ns_ms_local * 1e-3) / 1e12 if ns_ms_local > 0 else 0.0))
     launches = sm.launches_per_step() * args.steps
 
+    wait_profile = gemm_wait_profile(sm.step, dev) if args.gemm_profile else None
+
     # -------------------------------------------------------------- e2e run
     e2e = None
     if not args.no_e2e:
@@ -438,6 +440,8 @@ def run_ours(args, rank, world, local_rank):
         }
         if bar is not None:
             line["gpu_library_bar"] = bar
+        if wait_profile is not None:
+            line["gemm_wait_profile"] = wait_profile
         if world > 1:
             fl = [layout.flops(r) / 1e12 for r in range(world)]
             line["scaling_detail"] = {
@@ -456,6 +460,28 @@ def run_ours(args, rank, world, local_rank):
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def gemm_wait_profile(fn, dev) -> dict:
+    """One more (untimed) call of ``fn`` with the two-SM GEMM kernel's wait
+    counters on: the share of each role's time spent waiting (SM cycles summed
+    over CTAs)."""
+    from pytorch_opt_b200 import _lib
+    torch.cuda.synchronize(dev)
+    _lib.gemm_profile(True)          # zero, then switch on
+    fn()
+    c = _lib.gemm_profile(False)     # synchronise, read, switch off
+    def share(a, b):
+        return round(c[a] / c[b], 4) if c[b] else None
+    busy = c["mma_total"] - c["mma_full_wait"] - c["mma_tempty_wait"]
+    return {"mma_waits_for_operands": share("mma_full_wait", "mma_total"),
+            "mma_waits_for_accumulator": share("mma_tempty_wait", "mma_total"),
+            "producer_waits_for_stage": share("producer_empty_wait", "producer_total"),
+            "epilogue_waits_for_accumulator": share("epilogue_full_wait", "epilogue_total"),
+            "epilogue_working": share("epilogue_work", "epilogue_total"),
+            "tiles": c["tiles"],
+            "mma_issue_cycles_per_tile": round(busy / c["tiles"], 1) if c["tiles"] else None,
+            "how": "po_gemm_profile counters over one extra untimed call; clock64 cycles per role summed over CTAs"}
 
 
 # ------------------------------------------------- secondary workloads (1 GPU)
@@ -741,9 +767,12 @@ def run_secondary(args, rank):
             cpu = {"value": round(t * 1e3 * 4, 2), "unit": "ms", "cores": threads, "kind": "reference",
                    "sample": "the reference's ATen NS5 on one 4096^2 matrix of the workload, x4"}
         traffic, prof_fp, prof_match = profiled_traffic("tc_gemm_pair_ns4096.md")
+        extra = {"ms_per_step": round(ms, 4), "traffic_profiled_build": prof_fp, "traffic_matches_this_build": prof_match}
+        if args.gemm_profile:
+            extra["gemm_wait_profile"] = gemm_wait_profile(
+                lambda: native.newton_schulz_orthogonalize(G, 5, 3.4445, -4.7750, 2.0315, 1e-7), dev)
         _line(args, "NS5 4x4096^2 ms", ms, "ms", False, desc, fl / (ms * 1e-3) / 1e12, clk, (2 + 3 * 5) * args.steps,
-              cpu, {"ms_per_step": round(ms, 4), "traffic_profiled_build": prof_fp,
-                    "traffic_matches_this_build": prof_match}, traffic=traffic)
+              cpu, extra, traffic=traffic)
         return 0
     if w == "gemm":        # the product kernel alone, beside cuBLAS on the same shape
         import ctypes
@@ -800,6 +829,68 @@ def run_secondary(args, rank):
               "EKFAC QG (Vt / (s + 1e-3)) QA^T with Vt = QG^T V QA and the running scales updated in place, "
               "fp32 4096x4096, split-bf16 products", fl / (ms * 1e-3) / 1e12, clk, (4 + 3) * args.steps, cpu,
               {"ms_per_step": round(ms, 4)})
+        return 0
+    if w == "soap":        # section 8f rank 2: SOAP's basis refresh of one 1024x1024 matrix parameter
+        d = 1024
+        g = torch.Generator(device=dev).manual_seed(7)
+        Gs = [torch.randn(d, d, generator=g, device=dev) * 0.02 for _ in range(12)]
+        L = torch.zeros(d, d, device=dev)
+        R = torch.zeros(d, d, device=dev)
+        for k, G in enumerate(Gs):
+            L.mul_(0.95).add_(G @ G.T, alpha=0.05)
+            R.mul_(0.95).add_(G.T @ G, alpha=0.05)
+            if k == 1:
+                QLo = torch.linalg.eigh(L.double())[1].float()
+                QRo = torch.linalg.eigh(R.double())[1].float()
+        QLn = torch.linalg.eigh(L.double())[1].float()
+        QRn = torch.linalg.eigh(R.double())[1].float()
+        V0 = torch.rand(d, d, generator=g, device=dev) ** 2
+        V = V0.clone()
+        ms_tr, clk = _timed(lambda: native.soap_transport_(V, QLo, QLn, QRo, QRn), args.steps, args.warmup, dev, flush)
+        st = {"L": L, "R": R, "exp_avg_sq": V0.clone()}
+
+        def refresh(method):
+            st.update(Q_L=QLo, Q_R=QRo)
+            native.soap_refresh_(st, torch.float32, method, 1)
+        ms_sub, _ = _timed(lambda: refresh("subspace"), args.steps, args.warmup, dev, flush)
+        ms_eigh, _ = _timed(lambda: refresh("eigh"), args.steps, args.warmup, dev, flush)
+
+        def torch_refresh(Lx, Rx, QLx, QRx, Vx):  # the reference's lines (soap.py:98-108) on the given device
+            ql = torch.linalg.eigh(Lx.double())[1].float()
+            qr = torch.linalg.eigh(Rx.double())[1].float()
+            cl, cr = QLx.T @ ql, QRx.T @ qr
+            return cl.pow(2).T @ Vx @ cr.pow(2)
+        tf32 = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False  # the reference's fp32 matmuls
+        try:
+            ms_ref_gpu, _ = _timed(lambda: torch_refresh(L, R, QLo, QRo, V0), args.steps, args.warmup, dev, flush)
+        finally:
+            torch.backends.cuda.matmul.allow_tf32 = tf32
+        cpu = None
+        if not args.no_cpu_baseline:
+            Lc, Rc, QLc, QRc, Vc = (t.cpu() for t in (L, R, QLo, QRo, V0))
+            t = _cpu_time(lambda: torch_refresh(Lc, Rc, QLc, QRc, Vc))
+            cpu = {"value": round(t * 1e3, 1), "unit": "ms", "cores": threads, "kind": "reference",
+                   "sample": "the reference's refresh lines (soap.py:98-108: two fp64 eigh, the transport in fp32) "
+                             "on the same 1024x1024 factors, on the host"}
+        fl = 8.0 * d ** 3
+        _line(args, "SOAP refresh ms (1024x1024 parameter)", ms_sub, "ms", False,
+              "SOAP basis refresh of one 1024x1024 fp32 parameter: warm-started subspace iteration (1 iteration, "
+              "CholeskyQR2) for both factors plus the second-moment transport", fl / (ms_tr * 1e-3) / 1e12, clk,
+              37 * args.steps, cpu,
+              {"ms_per_step": round(ms_sub, 4), "dtype": "f32",
+               "transport_ms": round(ms_tr, 4),
+               "transport_tflops": round(fl / (ms_tr * 1e-3) / 1e12, 1),
+               "refresh_eigh_ms": round(ms_eigh, 3),
+               "reference_on_gpu_ms": round(ms_ref_gpu, 3),
+               "note": "refresh_eigh: the reference's fp64 eigh bases (library, on the GPU) with the transport on "
+                       "this library; reference_on_gpu: the reference's own lines on CUDA tensors (TF32 off); "
+                       "the subspace refresh approximates eigh's bases (exact on separated eigenvalues); roofline: "
+                       "the transport's four products (8 d^3 FLOPs) on split-tf32 operands",
+               "gpu_launches_note": "per refresh: 12 library kernels per basis (three products, each two operand "
+                                    "splits and one GEMM), 13 for the transport; plus cuSOLVER's Cholesky and "
+                                    "triangular solves"}, peak=peaks()["bf16_sustained"] / 6,
+              peak_name="bf16 sustained / 6 (split-tf32: three tf32 passes at half the bf16 rate)")
         return 0
     raise SystemExit(f"unknown workload {w}")
 
@@ -891,7 +982,8 @@ def main(argv=None) -> int:
                     help="single-GPU workloads repeat their timed calls until the timed region lasts this long "
                          "(so the clock sampler sees it); 0 times exactly --steps calls (for profiling)")
     ap.add_argument("--workload", default="llama8b",
-                    choices=("llama8b", "ns768", "ns4096", "gpt2", "shampoo", "kfac", "gemm", "ekfac", "kfac_split"),
+                    choices=("llama8b", "ns768", "ns4096", "gpt2", "shampoo", "kfac", "gemm", "ekfac", "kfac_split",
+                             "soap"),
                     help="llama8b (default, config 5); the others are single-GPU measurements of configs 1-4, "
                          "the 4x4096^2 profiling case and the bare product kernel (gemm)")
     ap.add_argument("--gemm", type=int, nargs=3, default=(8192, 8192, 8192), metavar=("M", "N", "K"),
@@ -899,6 +991,8 @@ def main(argv=None) -> int:
     ap.add_argument("--gemm-dtype", choices=("bf16", "tf32"), default="bf16")
     ap.add_argument("--kfac-split", choices=("factors", "bands"), default="factors",
                     help="--workload kfac_split: whole factors per rank, or row bands of each factor")
+    ap.add_argument("--gemm-profile", action="store_true",
+                    help="llama8b / ns4096: add the product kernel's wait-cycle shares from one extra untimed step")
     ap.add_argument("--exchange-chunks", type=int, default=None,
                     help="all-gather chunks per step for N > 1 (default 4; 1 = one all-gather after the local step)")
     args = ap.parse_args(argv)

@@ -46,6 +46,17 @@ const char* po_last_error(void);
  * and clears it when `reset` is nonzero. */
 int po_device_error(int reset);
 
+/* Measurement switch (no counterpart in the reference): while enabled, the
+ * two-SM GEMM kernel adds, per role and summed over CTAs, the SM clock cycles
+ * spent in its waits to 16 device counters (0: MMA issuer waiting for operand
+ * stages, 1: MMA issuer waiting for a free accumulator, 2: MMA issuer total,
+ * 3: TMA producer waiting for a free stage, 4: producer total, 5: first
+ * epilogue warp waiting for an accumulator, 6: its draining and storing,
+ * 7: its total, 8: tiles). With out != NULL, synchronises the device, copies
+ * the first n counters to out and zeroes them; then sets the switch to
+ * `enable`. Off by default; the counters cost a few clock reads per stage. */
+int po_gemm_profile(int enable, unsigned long long* out, int n);
+
 /* Library version string. */
 const char* po_version(void);
 
@@ -186,6 +197,20 @@ int po_precond_apply_norm(const void* L, long long l_ld, const void* G, long lon
 int po_precond_apply_ex(const void* L, long long l_ld, int trans_l, const void* G, long long g_ld, const void* R,
                         long long r_ld, int trans_r, void* out, long long out_ld, int dtype, long long m, long long n,
                         double* sq_sum, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * SOAP second-moment transport on a basis refresh: replaces
+ * pytorch_opt/optim/soap.py:101-108,
+ *   C_L = Q_L_old^T Q_L_new;  C_R = Q_R_old^T Q_R_new;
+ *   V <- (C_L o C_L)^T V (C_R o C_R)      (o: elementwise product),
+ * in place on V (m x n, pitch v_ld). Q_L_* m x m (pitch ql_ld), Q_R_* n x n
+ * (pitch qr_ld), all of `dtype` (PO_F32: split-tf32 products, fp32-grade;
+ * PO_BF16: bf16 products, squares rounded to bf16), row-major.
+ * ---------------------------------------------------------------------- */
+size_t po_soap_transport_workspace_bytes(long long m, long long n, int dtype);
+int po_soap_transport(const void* ql_old, const void* ql_new, long long ql_ld, const void* qr_old, const void* qr_new,
+                      long long qr_ld, void* v, long long v_ld, int dtype, long long m, long long n, void* workspace,
+                      size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
  * EKFAC preconditioning of one layer's gradient V (m x n, fp32): replaces

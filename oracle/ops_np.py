@@ -16,7 +16,7 @@ import numpy as np
 __all__ = [
     "bf16_round", "newton_schulz", "coupled_newton", "inverse_matrix_root", "kron_factor_update",
     "precond_apply", "kfac_batch_factors_linear", "kfac_update", "kfac_factored_damping",
-    "kfac_damped_inverse", "muon_scale", "muon_matrix_step", "root_residual",
+    "kfac_damped_inverse", "muon_scale", "muon_matrix_step", "root_residual", "soap_bases", "soap_transport",
 ]
 
 
@@ -228,6 +228,23 @@ def ekfac_precondition(QG, QA, V, scale, decay: float, damping: float):
     else:
         s = (np.asarray(scale, dtype=work) * work.type(decay) + work.type(1.0 - decay) * sq).astype(work)
     return (QG @ (Vt / (s + work.type(damping))) @ QA.T).astype(work), s
+
+
+def soap_bases(L, R, dtype=np.float32):
+    """SOAP's refreshed eigenbases (pytorch_opt/optim/soap.py:98-99): fp64
+    eigh, eigenvectors in ascending eigenvalue order, cast to the state dtype."""
+    ql = np.linalg.eigh(np.asarray(L, dtype=np.float64))[1].astype(dtype)
+    qr = np.linalg.eigh(np.asarray(R, dtype=np.float64))[1].astype(dtype)
+    return ql, qr
+
+
+def soap_transport(V, ql_old, ql_new, qr_old, qr_new) -> np.ndarray:
+    """SOAP's second-moment transport on a refresh (pytorch_opt/optim/soap.py:101-108):
+    C_L = Q_L_old^T Q_L_new, C_R = Q_R_old^T Q_R_new, V' = (C_L^2)^T V (C_R^2), in fp64."""
+    f = lambda x: np.asarray(x, dtype=np.float64)  # noqa: E731
+    cl = _mT(f(ql_old)) @ f(ql_new)
+    cr = _mT(f(qr_old)) @ f(qr_new)
+    return _mT(cl * cl) @ f(V) @ (cr * cr)
 
 
 def muon_scale(shape, lr_adjust: str = "spectral") -> float:

@@ -27,6 +27,7 @@ SIGNATURES = {
     "po_device_error": (_i, [_i]),
     "po_version": (ctypes.c_char_p, []),
     "po_selftest_wait_timeout": (_i, [ctypes.c_ulonglong, _i, _vp]),
+    "po_gemm_profile": (_i, [_i, _vp, _i]),
     "po_ns_workspace_bytes": (_sz, [_ll, _ll, _ll]),
     "po_newton_schulz": (_i, [_vp, _i, _ll, _ll, _ll, _ll, _ll, _vp, _ll, _ll, _i, _f, _f, _f, _f, _i, _vp, _sz,
                               _vp]),
@@ -42,6 +43,8 @@ SIGNATURES = {
     "po_precond_apply": (_i, [_vp, _ll, _vp, _ll, _vp, _ll, _vp, _ll, _i, _ll, _ll, _vp, _sz, _vp]),
     "po_precond_apply_norm": (_i, [_vp, _ll, _vp, _ll, _vp, _ll, _vp, _ll, _i, _ll, _ll, _vp, _vp, _sz, _vp]),
     "po_precond_apply_ex": (_i, [_vp, _ll, _i, _vp, _ll, _vp, _ll, _i, _vp, _ll, _i, _ll, _ll, _vp, _vp, _sz, _vp]),
+    "po_soap_transport_workspace_bytes": (_sz, [_ll, _ll, _i]),
+    "po_soap_transport": (_i, [_vp, _vp, _ll, _vp, _vp, _ll, _vp, _ll, _i, _ll, _ll, _vp, _sz, _vp]),
     "po_ekfac_workspace_bytes": (_sz, [_ll, _ll]),
     "po_ekfac_precondition": (_i, [_vp, _ll, _vp, _ll, _vp, _ll, _vp, _ll, _vp, _ll, _ll, _ll, _i, _f, _f, _vp, _sz,
                                    _vp]),
@@ -94,6 +97,21 @@ def check(status: int, what: str) -> None:
 def device_error(reset: bool = True) -> int:
     """Synchronise the current device and return (and clear) the device error word."""
     return int(load().po_device_error(1 if reset else 0))
+
+
+GEMM_PROFILE_SLOTS = ("mma_full_wait", "mma_tempty_wait", "mma_total", "producer_empty_wait", "producer_total",
+                      "epilogue_full_wait", "epilogue_work", "epilogue_total", "tiles")
+
+
+def gemm_profile(enable: bool, read: bool = True) -> dict | None:
+    """Switch the two-SM GEMM kernel's wait counters on or off; with `read`,
+    first return (and zero) what they have summed (SM clock cycles)."""
+    if not read:
+        check(load().po_gemm_profile(1 if enable else 0, None, 0), "po_gemm_profile")
+        return None
+    out = (ctypes.c_ulonglong * 16)()
+    check(load().po_gemm_profile(1 if enable else 0, ctypes.cast(out, ctypes.c_void_p), 16), "po_gemm_profile")
+    return {name: int(out[i]) for i, name in enumerate(GEMM_PROFILE_SLOTS)}
 
 
 def stream_ptr(device: torch.device | None = None) -> int:

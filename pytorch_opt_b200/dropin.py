@@ -24,8 +24,13 @@ make in the reference's sources to use the B200 kernels:
   on the rotated-diagonal kernel.
 * SOAP: ``SOAP._soap_update`` (``optim/soap.py:47-64``) receives its
   rotations into and out of the factors' eigenbases as the two-sided apply
-  kernel with transposed operands read in place (``soap.py:118-121``); the
-  eigenbases themselves stay the reference's fp64 ``eigh`` (``:98-110``).
+  kernel with transposed operands read in place (``soap.py:118-121``).
+  ``SOAP.step`` (``:66-131``) is restated with its basis refresh
+  (``:96-110``) as ``native.soap_refresh_``: the second-moment transport on
+  the tensor cores, the bases by the reference's fp64 ``eigh``
+  (``soap_refresh="eigh"``, the default) or by the warm-started subspace
+  iteration (``"subspace"``, an approximation; ``soap_refresh=None`` keeps
+  the reference's step).
 
 Every replacement falls through to the reference's original code for inputs
 this library does not serve (CPU tensors, fp64 factors), exactly as the
@@ -218,18 +223,91 @@ def _install_kfac(pytorch_opt) -> None:
     EKFAC._precondition = _eprecondition
 
 
-def install(pytorch_opt=None, kfac: bool = True) -> None:
+def _install_soap_step(pytorch_opt, method: str, iters: int) -> None:
+    """Restate ``SOAP.step`` (``optim/soap.py:66-131``) with the refresh on this library."""
+    import importlib
+    soap_mod = importlib.import_module(pytorch_opt.__name__ + ".optim.soap")
+    ops = importlib.import_module(pytorch_opt.__name__ + ".ops")
+    SOAP = soap_mod.SOAP
+    orig_step = SOAP.__dict__["step"]
+    timer, matrix_path, adamw_update = soap_mod.StepTimer, soap_mod.matrix_path, soap_mod.adamw_update
+
+    def refresh(p, st):
+        """soap.py:96-110: new bases of L and R, the rotated second moment carried into them."""
+        if _on_gpu(st["L"], st["R"]) and p.dtype in (torch.float32, torch.bfloat16):
+            native.soap_refresh_(st, p.dtype, method, iters)
+            return
+        QL = torch.linalg.eigh(st["L"].double())[1].to(p.dtype)
+        QR = torch.linalg.eigh(st["R"].double())[1].to(p.dtype)
+        if "Q_L" in st:
+            CL, CR = st["Q_L"].T @ QL, st["Q_R"].T @ QR
+            st["exp_avg_sq"] = CL.pow(2).T @ st["exp_avg_sq"] @ CR.pow(2)
+        st["Q_L"], st["Q_R"] = QL, QR
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        curvature_ms, stales, n_adamw = 0.0, [], 0
+        with timer() as t_all:
+            for group in self.param_groups:
+                for p in group["params"]:
+                    if p.grad is None:
+                        continue
+                    st = self.state[p]
+                    if not matrix_path(p, group):
+                        n_adamw += 1
+                        adamw_update(p, p.grad, st, group)
+                        continue
+                    g2 = p.grad.reshape(p.grad.shape[0], -1)
+                    m, n = g2.shape
+                    if "L" not in st:
+                        st.update(L=torch.zeros(m, m, device=p.device, dtype=p.dtype),
+                                  R=torch.zeros(n, n, device=p.device, dtype=p.dtype),
+                                  exp_avg=torch.zeros_like(g2), exp_avg_sq=torch.zeros_like(g2), step=0, stale=0)
+                    ops.kron_factor_update_(st["L"], st["R"], g2, beta2=group["shampoo_beta"])
+                    if st["step"] % group["precondition_frequency"] == 0:
+                        with timer() as t_c:
+                            refresh(p, st)
+                        curvature_ms += t_c.ms
+                        st["stale"] = 0
+                    else:
+                        st["stale"] += 1
+                    stales.append(st["stale"])
+                    QL, QR = st["Q_L"], st["Q_R"]
+                    self._soap_update(p.view(m, n), g2, st, group,
+                                      transform=lambda x, QL=QL, QR=QR: QL.T @ x @ QR,
+                                      back=lambda x, QL=QL, QR=QR: QL @ x @ QR.T)
+        self._diag = {"stale_steps": max(stales) if stales else 0, "n_adamw_params": n_adamw,
+                      "step_ms": t_all.ms, "curvature_ms": curvature_ms}
+        return loss
+
+    _SAVED["soap"] = [(SOAP, "step", orig_step)]
+    SOAP.step = step
+
+
+def install(pytorch_opt=None, kfac: bool = True, soap_refresh: str | None = "eigh", soap_iters: int = 1) -> None:
     """Install this library as ``pytorch_opt``'s native backend (and, with
-    ``kfac``, the KFAC rewiring). ``pytorch_opt``: the imported reference
-    package (imported here when omitted). Idempotent."""
+    ``kfac``, the KFAC and SOAP rewiring). ``pytorch_opt``: the imported
+    reference package (imported here when omitted). ``soap_refresh``: the
+    SOAP basis refresh (``"eigh"``: the reference's bases, transport on the
+    tensor cores; ``"subspace"``: ``native.soap_basis`` warm-started with
+    ``soap_iters`` iterations; None: the reference's ``SOAP.step``).
+    Idempotent; ``uninstall()`` first to change the options."""
     if pytorch_opt is None:
         import pytorch_opt
     from importlib import import_module
+    if soap_refresh not in (None, "eigh", "subspace"):
+        raise ValueError(f"unknown soap_refresh {soap_refresh!r}")
     ops = import_module(pytorch_opt.__name__ + ".ops")
     if "ops" not in _SAVED:
         _install_ops(ops)
     if kfac and "kfac" not in _SAVED:
         _install_kfac(pytorch_opt)
+        if soap_refresh is not None and "soap" not in _SAVED:
+            _install_soap_step(pytorch_opt, soap_refresh, soap_iters)
 
 
 def uninstall() -> None:
@@ -238,6 +316,6 @@ def uninstall() -> None:
         ops, saved = _SAVED.pop("ops")
         for k, v in saved.items():
             setattr(ops, k, v)
-    for owner, attr, orig in _SAVED.pop("kfac", []):
+    for owner, attr, orig in _SAVED.pop("kfac", []) + _SAVED.pop("soap", []):
         setattr(owner, attr, orig)
     _TRACES.clear()

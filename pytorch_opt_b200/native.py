@@ -324,6 +324,138 @@ def kfac_damped_inverse(F: torch.Tensor, gamma: float, max_iter: int = 100,
     return inv.to(F.dtype), cond
 
 
+def matmul(A: torch.Tensor, B: torch.Tensor, trans_a: bool = False, trans_b: bool = False,
+           out: torch.Tensor | None = None, alpha: float = 1.0, beta: float = 0.0) -> torch.Tensor:
+    """fp32 ``out = alpha op(A) op(B) + beta out`` on the tensor-core product
+    (``po_matmul``; op = transpose, read in place). fp32 operands run as
+    split-tf32 (fp32-grade), bf16 operands as bf16 products."""
+    dev = _require_cuda(A, B)
+    dt = A.dtype if A.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    Ac, Bc = A.to(dt).contiguous(), B.to(dt).contiguous()
+    M, K = (Ac.shape[1], Ac.shape[0]) if trans_a else tuple(Ac.shape)
+    N = Bc.shape[0] if trans_b else Bc.shape[1]
+    if (Bc.shape[1] if trans_b else Bc.shape[0]) != K:
+        raise RuntimeError("matmul: inner dimensions differ")
+    if out is None:
+        out = torch.zeros(M, N, dtype=torch.float32, device=dev) if beta else \
+            torch.empty(M, N, dtype=torch.float32, device=dev)
+    elif out.dtype != torch.float32 or tuple(out.shape) != (M, N) or not out.is_contiguous():
+        raise RuntimeError("matmul: out must be a contiguous fp32 M x N tensor")
+    if M and N and K:
+        with torch.cuda.device(dev):
+            lib = _lib.load()
+            code = _lib.DTYPE_CODE[dt]
+            prec = 2 if dt == torch.float32 else 0
+            nbytes = lib.po_matmul_workspace_bytes(1, M, N, K, code, prec)
+            ws = _lib.workspace(nbytes, dev)
+            _call("po_matmul", Ac.data_ptr(), Ac.shape[1], Ac.numel(), 1 if trans_a else 0, Bc.data_ptr(),
+                  Bc.shape[1], Bc.numel(), 1 if trans_b else 0, out.data_ptr(), N, M * N, code, prec, 1, M, N, K,
+                  float(alpha), float(beta), ws.data_ptr(), nbytes, _lib.stream_ptr(dev))
+    return out
+
+
+def soap_transport_(V: torch.Tensor, QL_old: torch.Tensor, QL_new: torch.Tensor, QR_old: torch.Tensor,
+                    QR_new: torch.Tensor) -> torch.Tensor:
+    """SOAP's second-moment transport (``pytorch_opt/optim/soap.py:101-108``),
+    in place: ``V <- (C_L o C_L)^T V (C_R o C_R)`` with ``C_L = QL_old^T QL_new``,
+    ``C_R = QR_old^T QR_new`` (``po_soap_transport``: two basis-change
+    products, a squaring pass and the two-sided apply with the transposed
+    left operand read in place)."""
+    dev = _require_cuda(V, QL_old, QL_new, QR_old, QR_new)
+    m, n = V.shape
+    dt = V.dtype
+    if dt not in (torch.float32, torch.bfloat16):
+        raise RuntimeError("soap_transport_: fp32 or bf16 state")
+    for Q, d in ((QL_old, m), (QL_new, m), (QR_old, n), (QR_new, n)):
+        if tuple(Q.shape) != (d, d) or Q.dtype != dt:
+            raise RuntimeError("soap_transport_: bases must be square, matching V's sides and dtype")
+    Vc = V if V.is_contiguous() else V.contiguous()
+    Qs = [Q.contiguous() for Q in (QL_old, QL_new, QR_old, QR_new)]
+    if m and n:
+        with torch.cuda.device(dev):
+            lib = _lib.load()
+            code = _lib.DTYPE_CODE[dt]
+            nbytes = lib.po_soap_transport_workspace_bytes(m, n, code)
+            ws = _lib.workspace(nbytes, dev)
+            _call("po_soap_transport", Qs[0].data_ptr(), Qs[1].data_ptr(), m, Qs[2].data_ptr(), Qs[3].data_ptr(), n,
+                  Vc.data_ptr(), n, code, m, n, ws.data_ptr(), nbytes, _lib.stream_ptr(dev))
+    if Vc is not V:
+        V.copy_(Vc)
+    return V
+
+
+def _cholesky_qr2(Y: torch.Tensor) -> torch.Tensor:
+    """Orthonormal basis of Y's columns, column order kept (the Q of Y = QR):
+    CholeskyQR twice, ``Y <- Y R^-1`` with ``R^T R = Y^T Y``; the Gram on the
+    tensor cores, the triangular factor and solve by the library. A Gram that
+    is not numerically positive definite gets a diagonal shift of 1e-6 of its
+    mean diagonal and one more pass (shifted CholeskyQR)."""
+    passes, k = 2, 0
+    while k < passes:
+        C = matmul(Y, Y, trans_a=True)
+        C = 0.5 * (C + C.mT)
+        R, info = torch.linalg.cholesky_ex(C, upper=True)
+        if int(info) != 0:
+            shift = 1e-6 * float(C.diagonal().mean().clamp_min(1e-30))
+            R = torch.linalg.cholesky(C + shift * torch.eye(C.shape[0], device=C.device), upper=True)
+            passes += 1
+        Y = torch.linalg.solve_triangular(R, Y, upper=True, left=False)
+        k += 1
+    return Y
+
+
+def soap_basis(F: torch.Tensor, Q_old: torch.Tensor | None = None, iters: int = 1, shift: float = 1e-3) -> torch.Tensor:
+    """Eigenbasis of a SOAP factor (``pytorch_opt/optim/soap.py:98-99``), columns
+    in ascending eigenvalue order like ``eigh``.
+
+    Without ``Q_old`` (the first refresh) it is the reference's own fp64
+    ``eigh`` on the device. With it, a warm-started subspace iteration: the
+    previous basis sorted by its Rayleigh quotients (descending), then
+    ``iters`` times ``Q <- qr((F + s I) Q)`` with ``s = shift * max|lambda|``
+    (same eigenvectors; it bounds the Gram's condition for CholeskyQR2), the
+    products on the tensor cores; finally the columns sorted by ascending
+    Rayleigh quotient. This is the power-iteration refresh of Vyas et al.
+    (SOAP, 2024), an approximation of the reference's exact ``eigh``: each
+    iteration contracts the angle between eigenvectors i and j by about
+    (lambda_j + s) / (lambda_i + s), so directions with well-separated
+    eigenvalues converge and those inside clusters stay approximate.
+    """
+    _require_cuda(F)
+    if Q_old is None:
+        return torch.linalg.eigh(F.double())[1].to(F.dtype)
+    if iters < 1:
+        raise ValueError("soap_basis: iters must be >= 1")
+    Q = Q_old.float()
+    Y = matmul(F, Q)
+    lam = (Q * Y).sum(0)
+    sigma = shift * float(lam.abs().max().clamp_min(1e-30))
+    order = torch.argsort(lam, descending=True)
+    Q, Y = Q[:, order].contiguous(), Y[:, order].contiguous()
+    for it in range(iters):
+        if it:
+            Y = matmul(F, Q)
+        Q = _cholesky_qr2(Y.add_(Q, alpha=sigma))
+    lam = (Q * matmul(F, Q)).sum(0)
+    return Q[:, torch.argsort(lam)].to(F.dtype)
+
+
+def soap_refresh_(st: dict, dtype: torch.dtype, method: str = "eigh", iters: int = 1) -> None:
+    """SOAP's basis refresh of one parameter's state (``pytorch_opt/optim/soap.py:96-110``):
+    new bases of ``st["L"]``, ``st["R"]`` (``method`` "eigh": the reference's
+    fp64 eigh; "subspace": ``soap_basis`` warm-started from the previous
+    bases), the rotated second moment transported into them on the
+    tensor cores (``soap_transport_``), then the bases replaced."""
+    if method not in ("eigh", "subspace"):
+        raise ValueError(f"unknown SOAP refresh method {method!r}")
+    old_l, old_r = st.get("Q_L"), st.get("Q_R")
+    warm = method == "subspace" and old_l is not None
+    QL = soap_basis(st["L"], old_l if warm else None, iters).to(dtype)
+    QR = soap_basis(st["R"], old_r if warm else None, iters).to(dtype)
+    if old_l is not None:
+        soap_transport_(st["exp_avg_sq"], old_l, QL, old_r, QR)
+    st["Q_L"], st["Q_R"] = QL, QR
+
+
 def newton_schulz_batched(Gs, steps: int = 5, coeffs=(3.4445, -4.7750, 2.0315), eps: float = 1e-7):
     """Orthogonalise many matrices: a 3-D tensor, or a list grouped by (shape, dtype) into batched launches."""
     a, b, c = coeffs

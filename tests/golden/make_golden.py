@@ -217,6 +217,30 @@ def make_ekfac() -> dict:
     return out
 
 
+def make_soap() -> dict:
+    """SOAP.step (optim/soap.py:66-131) on one fp32 matrix with a basis
+    refresh every step (precondition_frequency=1): the state after each of
+    three steps and the gradient of the next, so that a refresh's transport
+    (:101-108) can be checked from the state before and after it."""
+    from pytorch_opt.optim import SOAP
+    out = {}
+    m, n = 24, 40
+    g = torch.Generator().manual_seed(600)
+    p = torch.nn.Parameter(torch.randn(m, n, generator=g))
+    opt = SOAP([p], lr=3e-3, precondition_frequency=1)
+    grads = [torch.randn(m, n, generator=g) * 0.1 for _ in range(3)]
+    for k, gr in enumerate(grads):
+        p.grad = gr.clone()
+        opt.step()
+        st = opt.state[p]
+        snap = {"grad": gr, "L": st["L"], "R": st["R"], "QL": st["Q_L"], "QR": st["Q_R"], "V": st["exp_avg_sq"],
+                "p": p.detach()}
+        out.update({f"step{k}_{key}": _f32(t.clone()) for key, t in snap.items()})  # copies: the state is updated in place
+    out["hp"] = np.array([opt.param_groups[0]["betas"][1], opt.param_groups[0]["shampoo_beta"]], dtype=np.float64)
+    out["nsteps"] = np.array(len(grads))
+    return out
+
+
 def main(only=None) -> None:
     """Write every fixture, or only the named ones (e.g. ``ekfac``)."""
     R, KronTracker, kfac_factored_damping, KFAC, Muon = _import_reference()
@@ -225,7 +249,7 @@ def main(only=None) -> None:
         "ns": lambda: make_ns(R), "roots": lambda: make_roots(R), "kron": lambda: make_kron(R),
         "precond": lambda: make_precond(R),
         "kfac": lambda: make_kfac(KronTracker, kfac_factored_damping, KFAC), "muon": lambda: make_muon(Muon),
-        "ekfac": make_ekfac,
+        "ekfac": make_ekfac, "soap": make_soap,
     }
     for name, make in makers.items():
         if only and name not in only:

@@ -52,6 +52,18 @@ def _kfac_params(po):
     return [p.detach().clone() for p in model.parameters()], opt.diagnostics["mean_cond_A"]
 
 
+def _soap_params(po, **kw):
+    from pytorch_opt.optim import SOAP
+    torch.manual_seed(6)
+    params = [nn.Parameter(torch.randn(12, 20)), nn.Parameter(torch.randn(6, 3, 2, 2)), nn.Parameter(torch.randn(7))]
+    opt = SOAP(params, lr=3e-3, precondition_frequency=2, weight_decay=0.01, **kw)
+    for _ in range(5):
+        for p in params:
+            p.grad = torch.randn_like(p) * 0.1
+        opt.step()
+    return [p.detach().clone() for p in params], opt.diagnostics["stale_steps"], opt.diagnostics["n_adamw_params"]
+
+
 def test_cpu_tensors_keep_the_reference_path(po):
     from pytorch_opt import ops
     from pytorch_opt.optim import kfac as kfac_mod
@@ -61,8 +73,15 @@ def test_cpu_tensors_keep_the_reference_path(po):
                 soap_mod.SOAP.__dict__["_soap_update"])
     muon_ref = _muon_params(po)
     kfac_ref, cond_ref = _kfac_params(po)
+    soap_ref = _soap_params(po)
+    soap_step = soap_mod.SOAP.__dict__["step"]  # as torch's Optimizer wrapped it at the first construction
     dropin.install(po)
     try:
+        assert soap_mod.SOAP.__dict__["step"] is not soap_step  # the restated step (refresh on this library)
+        soap_got = _soap_params(po)
+        for a, b in zip(soap_got[0], soap_ref[0]):
+            assert torch.equal(a, b)
+        assert soap_got[1:] == soap_ref[1:]
         assert ops._NATIVE is native and ops.newton_schulz_orthogonalize is not before["newton_schulz_orthogonalize"]
         A = torch.randn(6, 6, dtype=torch.float64)
         A = A @ A.T + torch.eye(6, dtype=torch.float64)
@@ -80,3 +99,4 @@ def test_cpu_tensors_keep_the_reference_path(po):
         assert getattr(ops, k) is v
     assert (kfac_mod.kfac_factored_damping, kfac_mod.KFAC.__dict__["_damped_inverse"],
             soap_mod.SOAP.__dict__["_soap_update"]) == k_before
+    assert soap_mod.SOAP.__dict__["step"] is soap_step

@@ -171,17 +171,19 @@ def test_soap_dropin(po, cuda):
     entries stay negligible and the update is well defined."""
     from pytorch_opt.optim import SOAP
     shapes = [(64, 48), (40, 72), (200, 160)]
-    calls = []
-    orig = native.rotate_two_sided
+    calls, moved = [], []
+    orig, orig_tr = native.rotate_two_sided, native.soap_transport_
     native.rotate_two_sided = lambda *a, **k: calls.append(1) or orig(*a, **k)
+    native.soap_transport_ = lambda *a: moved.append(1) or orig_tr(*a)
     try:
         _, opt_r = _matrix_run(SOAP, shapes, 3, 3, "cpu", lr=3e-3, precondition_frequency=1)
         _, opt_g = _matrix_run(SOAP, shapes, 3, 3, cuda, lr=3e-3, precondition_frequency=1)
         ref, _ = _matrix_run(SOAP, shapes, 3, 3, "cpu", lr=3e-3, precondition_frequency=1, eps=1e-3)
         got, _ = _matrix_run(SOAP, shapes, 3, 3, cuda, lr=3e-3, precondition_frequency=1, eps=1e-3)
     finally:
-        native.rotate_two_sided = orig
+        native.rotate_two_sided, native.soap_transport_ = orig, orig_tr
     assert len(calls) == 2 * 3 * len(shapes) * 3  # transform(g), transform(m), back(update) per matrix, step, run
+    assert len(moved) == 2 * 2 * len(shapes)  # the refreshes of steps 2 and 3 transport the second moment
     ferr = []
     for pg, pr in zip(opt_g.param_groups[0]["params"], opt_r.param_groups[0]["params"]):
         sg, sr = opt_g.state[pg], opt_r.state[pr]
@@ -191,6 +193,47 @@ def test_soap_dropin(po, cuda):
           f"{[f'{e:.2e}' for e in errs]}")
     assert max(ferr) <= 1e-5
     assert max(errs) <= 1e-3
+
+
+def test_soap_dropin_subspace_refresh(po, cuda):
+    """``dropin.install(soap_refresh="subspace")``: after the first refresh
+    (fp64 eigh, nothing to start from) every refresh is the warm-started
+    subspace iteration (``native.soap_basis`` with the previous basis). The
+    factors still equal the reference's (they do not depend on the bases)
+    and the bases stay orthonormal to fp32 accuracy. How far the bases and
+    the parameters move from the eigh run's is printed, not bounded: on
+    these random factors even the top eigenvalues are close together, which
+    is where the iteration is an approximation (its convergence on separated
+    eigenvalues is asserted in ``test_gpu_soap.py``)."""
+    from pytorch_opt.optim import SOAP
+    shapes = [(64, 48), (200, 160)]
+    warm = []
+    orig = native.soap_basis
+    native.soap_basis = lambda F, Q_old=None, iters=1, **k: warm.append(Q_old is not None) or orig(F, Q_old, iters, **k)
+    dropin.uninstall()
+    dropin.install(po, soap_refresh="subspace", soap_iters=2)
+    try:
+        ref, opt_r = _matrix_run(SOAP, shapes, 3, 3, "cpu", lr=3e-3, precondition_frequency=1, eps=1e-3)
+        got, opt_g = _matrix_run(SOAP, shapes, 3, 3, cuda, lr=3e-3, precondition_frequency=1, eps=1e-3)
+    finally:
+        native.soap_basis = orig
+        dropin.uninstall()
+        dropin.install(po)
+    assert warm == [False, False] * len(shapes) + [True, True] * 2 * len(shapes)
+    tops = []
+    for pg, pr in zip(opt_g.param_groups[0]["params"], opt_r.param_groups[0]["params"]):
+        sg, sr = opt_g.state[pg], opt_r.state[pr]
+        assert _rel(sg["L"], sr["L"]) <= 1e-5 and _rel(sg["R"], sr["R"]) <= 1e-5
+        for F, Q in ((sg["L"], sg["Q_L"]), (sg["R"], sg["Q_R"])):
+            Q64, F64 = Q.double().cpu(), F.double().cpu()
+            assert float((Q64.T @ Q64 - torch.eye(Q64.shape[0], dtype=torch.float64)).abs().max()) <= 1e-5
+            ev, V = torch.linalg.eigh(F64)
+            tops.append(f"{float((Q64[:, -1] @ V[:, -1]).abs()):.3f} (gap {float((ev[-1] - ev[-2]) / ev[-1]):.2f})")
+    cos = [float((a.double().flatten() @ b.double().flatten()) / (a.double().norm() * b.double().norm()))
+           for a, b in zip(got, ref)]
+    assert all(torch.isfinite(a).all() for a in got)
+    print(f"SOAP subspace refresh: top-eigenvector |cos| vs eigh {tops}; parameter-change cosine vs the eigh run "
+          f"{[f'{c:.3f}' for c in cos]}")
 
 
 def _mlp():

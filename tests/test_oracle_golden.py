@@ -134,6 +134,28 @@ def test_ekfac_oracle_matches_reference_golden():
 
 
 
+def test_soap_refresh_oracle_matches_reference_golden():
+    """The reference's SOAP refreshed its bases every step; from the state
+    before and after each refresh: the oracle's bases are eigenbases of the
+    new factors matching the reference's up to column signs, and the
+    oracle's transport, followed by the step's second-moment EMA, gives the
+    reference's second moment."""
+    z = np.load(os.path.join(GOLDEN_DIR, "soap.npz"))
+    b2, _ = (float(v) for v in z["hp"])
+    for k in range(1, int(z["nsteps"])):
+        L, R = z[f"step{k}_L"], z[f"step{k}_R"]
+        ql, qr = O.soap_bases(L, R)
+        for mine, ref in ((ql, z[f"step{k}_QL"]), (qr, z[f"step{k}_QR"])):
+            cos = np.abs(np.sum(mine.astype(np.float64) * ref, axis=0))
+            assert cos.min() >= 1 - 1e-4, (k, cos.min())
+        ql, qr = z[f"step{k}_QL"].astype(np.float64), z[f"step{k}_QR"].astype(np.float64)
+        carried = O.soap_transport(z[f"step{k - 1}_V"], z[f"step{k - 1}_QL"], ql, z[f"step{k - 1}_QR"], qr)
+        g_rot = ql.T @ z[f"step{k}_grad"].astype(np.float64) @ qr
+        want = z[f"step{k}_V"]
+        got = b2 * carried + (1 - b2) * g_rot * g_rot
+        assert np.linalg.norm(got - want) / np.linalg.norm(want) <= 1e-5, k
+
+
 # --------------------------------------------------- torch full-size checker
 # oracle/ops_torch.py evaluates the same algorithms with torch (on the GPU in
 # the full-size parity tests); here it is pinned on the CPU to the same
