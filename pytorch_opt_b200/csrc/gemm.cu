@@ -5,6 +5,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -41,6 +42,26 @@ int* device_error_word() {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
     ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+
+// Wait-cycle counters of the two-SM kernel, filled while po_gemm_profile has
+// switched them on (measurement only).
+__device__ unsigned long long g_gemm_prof[kProfSlots];
+static std::atomic<bool> g_gemm_prof_on{false};
+
+unsigned long long* gemm_prof_word() {
+  if (!g_gemm_prof_on.load(std::memory_order_relaxed)) return nullptr;
+  static unsigned long long* ptrs[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_gemm_prof) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<unsigned long long*>(p);
   }
   return ptrs[dev];
 }
@@ -263,6 +284,7 @@ int launch_gemm(const GemmDesc& d, cudaStream_t stream) {
   P.sched = (pair && !(dyn_env != nullptr && dyn_env[0] == '0')) ? d.sched : nullptr;
   P.err = device_error_word();
   if (P.err == nullptr) return set_error(PO_ERR_CUDA, "device error word unavailable");
+  P.prof = pair ? gemm_prof_word() : nullptr;
   P.epi = d.epi;
 
   const bool a_mn = !d.a_kmajor, b_mn = !d.b_kmajor;
@@ -295,6 +317,23 @@ extern "C" int po_device_error(int reset) {
   if (cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
   if (reset && v != 0) cudaMemset(p, 0, sizeof(int));
   return v;
+}
+
+extern "C" int po_gemm_profile(int enable, unsigned long long* out, int n) {
+  if (out != nullptr) {
+    if (n < 0 || n > po::kProfSlots) return po::set_error(PO_ERR_ARG, "po_gemm_profile: n out of range");
+    void* p = nullptr;
+    if (int r = po::check_cuda(cudaGetSymbolAddress(&p, po::g_gemm_prof), "po_gemm_profile")) return r;
+    if (int r = po::check_cuda(cudaDeviceSynchronize(), "po_gemm_profile")) return r;
+    if (n > 0)
+      if (int r = po::check_cuda(cudaMemcpy(out, p, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost),
+                                 "po_gemm_profile"))
+        return r;
+    if (int r = po::check_cuda(cudaMemset(p, 0, po::kProfSlots * sizeof(unsigned long long)), "po_gemm_profile"))
+      return r;
+  }
+  po::g_gemm_prof_on.store(enable != 0);
+  return PO_OK;
 }
 
 extern "C" const char* po_version(void) { return "pytorch_opt_b200 0.1 (sm_100a)"; }

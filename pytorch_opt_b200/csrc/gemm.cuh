@@ -160,7 +160,24 @@ struct alignas(64) GemmParams {
   const int* active;  // per batch: nonzero = compute (nullable: all)
   const int* passes;  // per batch pass count (nullable: npass)
   int* err;           // device error word
+  // Measurement only (nullable): cycles each role of the two-SM kernel spends
+  // in its waits, summed over CTAs (see po_gemm_profile).
+  unsigned long long* prof;
   Epilogue epi;
+};
+
+// Slots of GemmParams::prof.
+enum GemmProf : int {
+  kProfMmaFullWait = 0,    // MMA issuer waiting for operand stages (TMA not ahead)
+  kProfMmaTemptyWait = 1,  // MMA issuer waiting for a free accumulator (epilogue behind)
+  kProfMmaTotal = 2,       // MMA issuer's whole loop
+  kProfProdEmptyWait = 3,  // TMA producer waiting for a free stage (MMA behind)
+  kProfProdTotal = 4,
+  kProfEpiFullWait = 5,    // epilogue waiting for an accumulator (MMA behind)
+  kProfEpiWork = 6,        // epilogue draining and storing tiles
+  kProfEpiTotal = 7,
+  kProfTiles = 8,          // tiles processed (by the MMA issuers)
+  kProfSlots = 16
 };
 
 template <int KIND, int BN>

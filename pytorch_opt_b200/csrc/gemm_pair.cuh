@@ -129,6 +129,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
       uint32_t phase = 0;
       bool ok = true;
       uint32_t armed = 0;
+      const long long prof_t0 = P.prof != nullptr ? clock64() : 0;
+      long long prof_empty = 0;
       for (int j = 0; ok; ++j) {
         int t;
         if (leader) {
@@ -155,7 +157,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
         for (int v = 0; v < nv; ++v) {
           const int pass = v / nkb;
           const int k0 = (v - pass * nkb) * C::BK;
-          if (!mbar_wait_bounded(empty + stage, phase ^ 1u, abort_flag, P.err, kErrTimeoutProducer)) {
+          const long long pw0 = P.prof != nullptr ? clock64() : 0;
+          const bool got_empty = mbar_wait_bounded(empty + stage, phase ^ 1u, abort_flag, P.err, kErrTimeoutProducer);
+          if (P.prof != nullptr) prof_empty += clock64() - pw0;
+          if (!got_empty) {
             ok = false;
             break;
           }
@@ -195,6 +200,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
           }
         }
       }
+      if (P.prof != nullptr) {
+        atomicAdd(P.prof + kProfProdEmptyWait, static_cast<unsigned long long>(prof_empty));
+        atomicAdd(P.prof + kProfProdTotal, static_cast<unsigned long long>(clock64() - prof_t0));
+      }
       if (!ok && leader) {
         // The leader's full barrier counts both CTAs' bytes: once the last
         // arming of each stage completes, no load of either CTA is in flight.
@@ -229,6 +238,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
       uint32_t phase = 0;
       int ucount = 0;
       bool ok = true;
+      const long long prof_t0 = P.prof != nullptr ? clock64() : 0;
+      long long prof_full = 0, prof_tempty = 0;
       for (int j = 0; ok; ++j) {
         int t;
         if (!sched_read(sfull, stile, j, abort_flag, P.err, kErrTimeoutMma, t)) break;
@@ -239,11 +250,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
         const int nv = tile_passes(P, tc.b) * nkb;
         const int acc = ucount & 1;
         const uint32_t acc_phase = (ucount >> 1) & 1;
-        if (!mbar_wait_bounded_cluster(tempty + acc, acc_phase ^ 1u, abort_flag, P.err, kErrTimeoutMma)) break;
+        const long long tw0 = P.prof != nullptr ? clock64() : 0;
+        const bool got_acc = mbar_wait_bounded_cluster(tempty + acc, acc_phase ^ 1u, abort_flag, P.err, kErrTimeoutMma);
+        if (P.prof != nullptr) prof_tempty += clock64() - tw0;
+        if (!got_acc) break;
         tc_fence_after_sync();
         const uint32_t dtmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int v = 0; v < nv; ++v) {
-          if (!mbar_wait_bounded(full + stage, phase, abort_flag, P.err, kErrTimeoutMma)) {
+          const long long fw0 = P.prof != nullptr ? clock64() : 0;
+          const bool got_full = mbar_wait_bounded(full + stage, phase, abort_flag, P.err, kErrTimeoutMma);
+          if (P.prof != nullptr) prof_full += clock64() - fw0;
+          if (!got_full) {
             ok = false;
             break;
           }
@@ -272,6 +289,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
         mma_commit_pair_mc(tfull + acc, 0x3);
         ++ucount;
       }
+      if (P.prof != nullptr) {
+        atomicAdd(P.prof + kProfMmaFullWait, static_cast<unsigned long long>(prof_full));
+        atomicAdd(P.prof + kProfMmaTemptyWait, static_cast<unsigned long long>(prof_tempty));
+        atomicAdd(P.prof + kProfMmaTotal, static_cast<unsigned long long>(clock64() - prof_t0));
+        atomicAdd(P.prof + kProfTiles, static_cast<unsigned long long>(ucount));
+      }
       mma_commit_pair(drain);
       {
         const unsigned long long t0 = global_timer_ns();
@@ -290,6 +313,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
     constexpr int HC = BN / EC / 2;
     const int c_lo = ((warp - 2) >> 2) * HC;
     int ucount = 0;
+    const bool prof_on = P.prof != nullptr && warp == 2 && lane == 0;
+    const long long prof_t0 = prof_on ? clock64() : 0;
+    long long prof_wait = 0, prof_work = 0;
     for (int j = 0;; ++j) {
       int t;
       const bool got = sched_read(sfull, stile, j, abort_flag, P.err, kErrTimeoutEpilogue, t);
@@ -305,7 +331,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
       epilogue_prefetch(P, tc.b, row, tc.nt * BN + c_lo * EC, HC * EC);
       const int acc = ucount & 1;
       const uint32_t acc_phase = (ucount >> 1) & 1;
+      const long long ew0 = prof_on ? clock64() : 0;
       const bool ready = mbar_wait_bounded_sleep(tfull + acc, acc_phase, abort_flag, P.err, kErrTimeoutEpilogue);
+      const long long ew1 = prof_on ? clock64() : 0;
+      if (prof_on) prof_wait += ew1 - ew0;
       if (!__all_sync(0xffffffffu, ready)) break;
       tc_fence_after_sync();
 #pragma unroll 1
@@ -321,6 +350,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(tempty + acc), 0));
+      if (prof_on) prof_work += clock64() - ew1;
       ++ucount;
       if (P.epi.red_absmax != nullptr) {
 #pragma unroll
@@ -332,6 +362,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __g
         for (int o = 16; o > 0; o >>= 1) red += __shfl_xor_sync(0xffffffffu, red, o);
         if (lane == 0) atomicAdd(P.epi.red_sumsq + (P.epi.red_sumsq_shared ? 0 : tc.b), static_cast<double>(red));
       }
+    }
+    if (prof_on) {
+      atomicAdd(P.prof + kProfEpiFullWait, static_cast<unsigned long long>(prof_wait));
+      atomicAdd(P.prof + kProfEpiWork, static_cast<unsigned long long>(prof_work));
+      atomicAdd(P.prof + kProfEpiTotal, static_cast<unsigned long long>(clock64() - prof_t0));
     }
   }
 
