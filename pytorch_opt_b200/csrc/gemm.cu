@@ -236,6 +236,7 @@ int launch_gemm(const GemmDesc& d, cudaStream_t stream) {
   const int bk = 128 / es;
   // Rows of A and of B one CTA loads per stage; the two-SM kernel's stages
   // hold two 128-byte K atoms (MN-major boxes span 2 * bk rows of K).
+  const int kbox = pair ? 2 * bk : bk;
   const int a_rows = 128, b_rows = pair ? bn / 2 : bn;
   // MN-major 32-bit operands: 128 B swizzle with 32 B granules (the only
   // shared-memory layout the tensor cores accept for MN-major tf32).
@@ -246,19 +247,19 @@ int launch_gemm(const GemmDesc& d, cudaStream_t stream) {
   P.a4d = !d.a_kmajor && !no_mn4d;
   P.b4d = !d.b_kmajor && !no_mn4d;
   for (int i = 0; i < nmaps; ++i) {
-    if (P.a4d && encode_map_mn4d(&P.mapA[i], d.a[i], d.batch, pair ? 2 * bk : bk, a_rows * es / 128, mn_swz)) P.a4d = 0;
-    if (P.b4d && encode_map_mn4d(&P.mapB[i], d.b[i], d.batch, pair ? 2 * bk : bk, b_rows * es / 128, mn_swz)) P.b4d = 0;
+    if (P.a4d && encode_map_mn4d(&P.mapA[i], d.a[i], d.batch, kbox, a_rows * es / 128, mn_swz)) P.a4d = 0;
+    if (P.b4d && encode_map_mn4d(&P.mapB[i], d.b[i], d.batch, kbox, b_rows * es / 128, mn_swz)) P.b4d = 0;
   }
   for (int i = 0; i < 2; ++i) {
     const int src = i < nmaps ? i : 0;
     int r = 0;
     // A: logical M x K.
     if (d.a_kmajor) r = encode_map(&P.mapA[i], d.a[src], d.batch, bk, a_rows);
-    else if (!P.a4d) r = encode_map(&P.mapA[i], d.a[src], d.batch, 128 / es, pair ? 2 * bk : bk, mn_swz);
+    else if (!P.a4d) r = encode_map(&P.mapA[i], d.a[src], d.batch, 128 / es, kbox, mn_swz);
     else if (i >= nmaps) P.mapA[i] = P.mapA[0];
     if (r) return r;
     if (d.b_kmajor) r = encode_map(&P.mapB[i], d.b[src], d.batch, bk, b_rows);
-    else if (!P.b4d) r = encode_map(&P.mapB[i], d.b[src], d.batch, 128 / es, pair ? 2 * bk : bk, mn_swz);
+    else if (!P.b4d) r = encode_map(&P.mapB[i], d.b[src], d.batch, 128 / es, kbox, mn_swz);
     else if (i >= nmaps) P.mapB[i] = P.mapB[0];
     if (r) return r;
   }

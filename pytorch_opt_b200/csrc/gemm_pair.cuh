@@ -21,18 +21,18 @@
 
 namespace po {
 
-template <int KIND>
+template <int KIND, int ATOMS_ = 2>
 struct PairCfg {
   static constexpr int TM = 256;                          // rows per pair tile
   static constexpr int BN = 256;                          // columns per tile
   static constexpr int ES = (KIND == KIND_BF16) ? 2 : 4;
-  static constexpr int ATOMS = 2;                         // 128-byte swizzle atoms of K per stage
+  static constexpr int ATOMS = ATOMS_;                    // 128-byte swizzle atoms of K per stage
   static constexpr int AK = 128 / ES;                     // K elements per atom
   static constexpr int BK = ATOMS * AK;
   static constexpr int A_BYTES = 128 * 128 * ATOMS;       // this CTA's 128 rows of A
   static constexpr int B_BYTES = (BN / 2) * 128 * ATOMS;  // this CTA's half of B
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // per CTA
-  static constexpr int STAGES = 3;
+  static constexpr int STAGES = 6 / ATOMS;               // 192 KB of stages per CTA either way
   static constexpr int MMA_K = (KIND == KIND_BF16) ? 16 : 8;
   static constexpr int KSTEPS = BK / MMA_K;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
@@ -65,9 +65,9 @@ __device__ __forceinline__ void sched_release(uint64_t* sempty, int j) {
   mbar_arrive_cluster(mapa_shared(smem_u32(sempty + j % kSchedSlots), 0));
 }
 
-template <int KIND, bool A_MN, bool B_MN>
+template <int KIND, bool A_MN, bool B_MN, int ATOMS>
 __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_pair_kernel(const __grid_constant__ GemmParams P) {
-  using C = PairCfg<KIND>;
+  using C = PairCfg<KIND, ATOMS>;
   constexpr int BN = C::BN;
 
   extern __shared__ uint8_t smem_raw[];

@@ -10,10 +10,10 @@ namespace po {
 // Persistent launch: one cluster per co-resident CTA pair, capped by what the
 // occupancy query allows on this device (clusters are placed inside one GPC,
 // so this can be below SMs / 2).
-template <int KIND, bool A_MN, bool B_MN>
+template <int KIND, bool A_MN, bool B_MN, int ATOMS>
 int launch_pair_inst(const GemmParams& P, cudaStream_t stream) {
-  using C = PairCfg<KIND>;
-  auto kern = tc_gemm_pair_kernel<KIND, A_MN, B_MN>;
+  using C = PairCfg<KIND, ATOMS>;
+  auto kern = tc_gemm_pair_kernel<KIND, A_MN, B_MN, ATOMS>;
   static int max_pairs[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -45,12 +45,15 @@ int launch_pair_inst(const GemmParams& P, cudaStream_t stream) {
   return check_cuda(cudaLaunchKernelEx(&cfg, kern, P), "tc_gemm_pair launch");
 }
 
+// Three 64 KB stages of two 128-byte K atoms each (PairCfg's default). Six
+// 32 KB stages of one atom were measured slower on the Llama step (487 ms
+// against 463 ms on one box, at a higher clock: the tensor pipes idled more).
 template <int KIND>
 int dispatch_pair(const GemmParams& P, bool a_mn, bool b_mn, cudaStream_t s) {
-  if (!a_mn && !b_mn) return launch_pair_inst<KIND, false, false>(P, s);
-  if (!a_mn && b_mn) return launch_pair_inst<KIND, false, true>(P, s);
-  if (a_mn && !b_mn) return launch_pair_inst<KIND, true, false>(P, s);
-  return launch_pair_inst<KIND, true, true>(P, s);
+  if (!a_mn && !b_mn) return launch_pair_inst<KIND, false, false, 2>(P, s);
+  if (!a_mn && b_mn) return launch_pair_inst<KIND, false, true, 2>(P, s);
+  if (a_mn && !b_mn) return launch_pair_inst<KIND, true, false, 2>(P, s);
+  return launch_pair_inst<KIND, true, true, 2>(P, s);
 }
 
 extern template int dispatch_pair<KIND_BF16>(const GemmParams&, bool, bool, cudaStream_t);
