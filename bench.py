@@ -98,7 +98,7 @@ def peaks():
 class ClockSampler:
     """nvidia-smi clock / throttle-reason sampling while the timed region runs."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
     REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
@@ -106,6 +106,7 @@ class ClockSampler:
     def __init__(self, device: torch.device):
         self.proc = None
         self.path = None
+        self.t_begin = self.t_end = None
         try:
             uuid = str(torch.cuda.get_device_properties(device).uuid)
             self.gpu = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
@@ -113,6 +114,8 @@ class ClockSampler:
             self.gpu = str(device.index or 0)
 
     def start(self):
+        """Start sampling every 200 ms and wait (up to 5 s) for the first sample,
+        so that a timed region marked afterwards is covered from its start."""
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
@@ -121,32 +124,56 @@ class ClockSampler:
                                          stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < 5.0 and self.proc.poll() is None and os.path.getsize(self.path) == 0:
+            time.sleep(0.02)
+
+    def mark_begin(self):
+        self.t_begin = time.time()
+
+    def mark_end(self):
+        self.t_end = time.time()
 
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        if self.t_end is None:
+            self.mark_end()
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-        sms, maxes, reasons = [], [], set()
+        rows = []
         with open(self.path) as f:
             for line in f:
                 parts = [x.strip() for x in line.split(",")]
-                if len(parts) < 9:
+                if len(parts) < 10:
                     continue
                 try:
-                    sms.append(float(parts[1]))
-                    maxes.append(float(parts[2]))
+                    ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                    rows.append((ts, float(parts[2]), float(parts[3]), parts[6:10]))
                 except ValueError:
                     continue
-                for name, val in zip(self.REASONS, parts[5:9]):
-                    if val.lower().startswith("active"):
-                        reasons.add(name)
         os.unlink(self.path)
-        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max(maxes) if maxes else None,
-                "reasons": sorted(reasons), "samples": len(sms)}
+        lo = (self.t_begin if self.t_begin is not None else -math.inf) - 0.05
+        hi = self.t_end + 0.25  # a sample is taken up to 200 ms after the state it reports
+        inside = [r for r in rows if lo <= r[0] <= hi]
+        how = "samples taken during the timed region"
+        if not inside and rows and self.t_begin is not None:  # region shorter than the sampling period
+            mid = 0.5 * (self.t_begin + self.t_end)
+            inside = [min(rows, key=lambda r: abs(r[0] - mid))]
+            how = f"timed region ({self.t_end - self.t_begin:.2f} s) shorter than the 200 ms period: nearest sample"
+        reasons = set()
+        for r in inside:
+            for name, val in zip(self.REASONS, r[3]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        sms = [r[1] for r in inside]
+        return {"sm_mhz": statistics.median(sms) if sms else None,
+                "sm_max_mhz": max(r[2] for r in inside) if inside else None,
+                "reasons": sorted(reasons), "samples": len(sms), "how": how}
 
 
 # ----------------------------------------------------------- CPU baseline
@@ -299,12 +326,35 @@ def gpu_library_bar(mats: list, dev: torch.device) -> dict:
     return out
 
 
+def gpu_local_cpus(dev: torch.device) -> set | None:
+    """Host CPUs on the NUMA node of the GPU's PCI device (sysfs), or None."""
+    try:
+        pr = torch.cuda.get_device_properties(dev)
+        addr = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{addr}/local_cpulist") as f:
+            spec = f.read().strip()
+        cpus = set()
+        for part in spec.split(","):
+            a, _, b = part.partition("-")
+            cpus.update(range(int(a), int(b or a) + 1))
+        return cpus & os.sched_getaffinity(0) or None
+    except (OSError, ValueError, AttributeError):
+        return None
+
+
 def run_ours(args, rank, world, local_rank):
     from pytorch_opt_b200.dist import ShardLayout, ShardedMuon
     import torch.distributed as dist
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    if world > 1 and os.environ.get("PO_BENCH_NUMA", "0") == "1":
+        # PO_BENCH_NUMA=1 (measurement switch): run each rank on its GPU's own
+        # NUMA node, so that the pinned gradient buffer of the end-to-end run
+        # (first touch) sits in the memory next to the GPU's PCIe link.
+        cpus = gpu_local_cpus(dev)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     shapes = llama_shapes()
@@ -336,19 +386,21 @@ def run_ours(args, rank, world, local_rank):
         return out.tolist()
 
     # ---------------------------------------------------- device-resident run
+    clocks = ClockSampler(dev)
+    clocks.start()
     for _ in range(args.warmup):
         sm.step()
     barrier()
-    clocks = ClockSampler(dev)
-    clocks.start()
     ns_events: list = []
     tail_events: list = []
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.mark_begin()
     e0.record(stream)
     for _ in range(args.steps):
         sm.step(ns_events, tail_events)
     e1.record(stream)
     barrier()
+    clocks.mark_end()
     clk = clocks.stop()
     step_ranks = all_ranks(e0.elapsed_time(e1) / args.steps)
     step_ms = max(step_ranks)
@@ -496,12 +548,13 @@ def _timed(fn, steps, warmup, dev, flush=None, min_seconds=None):
     sees it; the time is the mean over every timed call."""
     if min_seconds is None:
         min_seconds = MIN_TIMED_SECONDS
+    clocks = ClockSampler(dev)
+    clocks.start()
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize(dev)
-    clocks = ClockSampler(dev)
-    clocks.start()
     pairs = []
+    clocks.mark_begin()
     t0 = time.perf_counter()
     while True:
         for _ in range(steps):
@@ -515,6 +568,7 @@ def _timed(fn, steps, warmup, dev, flush=None, min_seconds=None):
         torch.cuda.synchronize(dev)
         if time.perf_counter() - t0 >= min_seconds or len(pairs) >= 200 * steps:
             break
+    clocks.mark_end()
     clk = clocks.stop()
     clk["timed_calls"] = len(pairs)
     return sum(a.elapsed_time(b) for a, b in pairs) / len(pairs), clk
@@ -927,15 +981,17 @@ def run_kfac_split(args, rank, world, local_rank):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
-    barrier()
     clocks = ClockSampler(dev)
     clocks.start()
+    barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.mark_begin()
     e0.record()
     for _ in range(args.steps):
         update()
     e1.record()
     barrier()
+    clocks.mark_end()
     clk = clocks.stop()
     ms = e0.elapsed_time(e1) / args.steps
     if world > 1:
