@@ -124,6 +124,17 @@ struct Epilogue {
   // alpha d_i^2 = alpha*(A A) + beta0*A.
   const float* dsym;
   long long dsym_bs;
+  // Product S T of two symmetric matrices held split (nullable s2_ds = off):
+  // the operands are F_S, F_T (zero diagonals), s2_fs / s2_ft the same bf16
+  // arrays read by rows, s2_ds / s2_dt their diagonals ([batch][M], plus the
+  // constants s2_ds_add / s2_dt_add: P = a I + B keeps B's arrays). The
+  // epilogue forms alpha*(acc + d_S,i F_T,ij + F_S,ij d_T,j + [i==j] d_S,i d_T,i)
+  // = alpha*(S T); with S, T polynomials in one matrix S T is symmetric.
+  EpiIn s2_fs, s2_ft;
+  const float* s2_ds;
+  const float* s2_dt;
+  long long s2_d_bs;
+  float s2_ds_add, s2_dt_add;
   // Per-batch scales read on the device (nullable): alpha is multiplied by
   // alpha_scale[b], in[0]'s coefficient (beta, plus in0_rowcoef) by in_scale[b].
   const float* alpha_scale;
@@ -605,7 +616,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCo
   if (row >= P.M) return;
   const int jd = row - col0;  // diagonal column within this chunk, if any
   float v[EC];
-  const bool same = E.diag_split || E.mirror_same || E.dsym != nullptr;
+  const bool same = E.diag_split || E.mirror_same || E.dsym != nullptr || E.s2_ds != nullptr;
   if (mirror && !same) {
     // Element (row, c) of an off-diagonal tile of a symmetric product is also
     // element (c, row): rebuild it with the addends read at (c, row) and
@@ -654,6 +665,21 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& P, const TileCo
       const float vj = (col0 + j < N) ? V[static_cast<long long>(col0 + j) * (E.dV.ld + 1)] : 0.0f;
       float t = fmaf(u, vr[j], ur[j] * vj);
       if (j == jd) t -= u * vj;
+      v[j] = fmaf(alpha, t, v[j]);
+    }
+  }
+  if (E.s2_ds != nullptr) {
+    const long long db = static_cast<long long>(tc.b) * E.s2_d_bs;
+    const float dsi = E.s2_ds[db + row] + E.s2_ds_add;
+    float fs[EC], ft[EC], dtj[EC];
+    load_row_any(E.s2_fs, tc.b, row, col0, N, fs);
+    load_row_any(E.s2_ft, tc.b, row, col0, N, ft);
+    load_vec_f32(E.s2_dt + db, col0, N, dtj);
+#pragma unroll
+    for (int j = 0; j < EC; ++j) {
+      const float dt = dtj[j] + E.s2_dt_add;
+      float t = fmaf(dsi, ft[j], fs[j] * dt);
+      if (j == jd) t = fmaf(dsi, dt, t);
       v[j] = fmaf(alpha, t, v[j]);
     }
   }

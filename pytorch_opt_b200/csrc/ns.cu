@@ -31,6 +31,8 @@
 // with the split). Matrices with m < 256 run every step on split-bf16 pairs
 // (hi*hi + hi*lo + lo*hi) with chunked accumulation, which keeps even long
 // or oscillating schedules close to the fp32 reference.
+#include <cstdlib>
+
 #include "elementwise.cuh"
 #include "gemm_host.cuh"
 
@@ -57,7 +59,23 @@ struct NsBuffers {
   double* sums;             // per-matrix sum of squares
   unsigned int* sched;      // tile queue of the products
   long long ldx, ldm, msz;  // msz: elements of one [batch][m][ldm] array
+  // Grouped steps (grouped_shape): bf16 zero-diagonal operands of P^2 and of
+  // the running product Q (ping-pong), and the second diagonals.
+  __nv_bfloat16* fp2;
+  __nv_bfloat16* fq[2];
+  float* adiag2;            // diag of the other A operand (A ping-pongs between a_hi and a_lo)
+  float* bdiag2;            // diag of the other B (P = a I + B ping-pongs between b_hi and b_lo)
+  float* p2diag;
+  float* qdiag[2];
 };
+
+// Shapes whose steps run in groups (see ns_core): far from square, so that
+// one tall product per group and a few m x m products cost less than a tall
+// Gram and update per step.
+inline bool grouped_shape(long long rows, long long cols) {
+  const long long m = rows < cols ? rows : cols, n = rows < cols ? cols : rows;
+  return m >= 256 && n >= 2 * m;
+}
 
 // X is kept in G's orientation: [rows][ldx], ldx = cols rounded up to 64.
 void ns_layout(Arena& ar, long long batch, long long rows, long long cols, bool split, NsBuffers& B) {
@@ -79,6 +97,17 @@ void ns_layout(Arena& ar, long long batch, long long rows, long long cols, bool 
   B.scale = static_cast<float*>(ar.take(static_cast<size_t>(batch) * 8));
   B.sums = static_cast<double*>(ar.take(static_cast<size_t>(batch) * 8));
   B.sched = take_sched(ar);
+  B.fp2 = B.fq[0] = B.fq[1] = nullptr;
+  B.adiag2 = B.bdiag2 = B.p2diag = B.qdiag[0] = B.qdiag[1] = nullptr;
+  if (grouped_shape(rows, cols)) {
+    B.fp2 = static_cast<__nv_bfloat16*>(ar.take(ms * 2));
+    for (int i = 0; i < 2; ++i) B.fq[i] = static_cast<__nv_bfloat16*>(ar.take(ms * 2));
+    const size_t vs = static_cast<size_t>(batch * m) * 4;
+    B.adiag2 = static_cast<float*>(ar.take(vs));
+    B.bdiag2 = static_cast<float*>(ar.take(vs));
+    B.p2diag = static_cast<float*>(ar.take(vs));
+    for (int i = 0; i < 2; ++i) B.qdiag[i] = static_cast<float*>(ar.take(vs));
+  }
 }
 
 int out_kind_of(int dtype) {
@@ -274,9 +303,31 @@ int ns_core(const void* G, int dtype, long long batch, long long rows, long long
   gv.cols = cols;
   gv.ld = ld;
   gv.bstride = bstride;
+  // Grouped steps. For a matrix far from square, the steps of a group share
+  // one tall Gram and one tall update: with A_0 = X^T X (tall; X X^T wide) and
+  // P_j = a I + b A_j + c A_j^2, the next Gram is A_{j+1} = A_j P_j^2 (P_j is a
+  // polynomial in A_j) and the group's update is X <- X P_0 P_1 ... (P_j ...
+  // X for wide matrices), so the steps inside a group cost m x m products
+  // only. Groups of three steps, the last group what is left (5 = 3 + 2);
+  // every m x m product keeps the diagonal split (operands with zeroed
+  // diagonals, the split-product epilogue adds the diagonal terms in fp32).
+  // Emulated in bf16 against the fp64 reference on 3584 x 1024 matrices
+  // (randn and a k^-1/2 spectrum): 5.9e-3 and 7.4e-3, against 5.7e-3 and
+  // 7.2e-3 for one Gram and update per step. PO_NS_GROUP=0 in the
+  // environment runs one Gram and update per step (for measurement).
+  const char* grp_env = getenv("PO_NS_GROUP");
+  const bool grouping = !split && tf32_tail == 0 && B.fp2 != nullptr && !(grp_env != nullptr && grp_env[0] == '0');
+  auto group_at = [&](int it) -> int {
+    if (!grouping) return 1;
+    const int left = steps - it;
+    return left >= 3 ? 3 : left;
+  };
+  auto bview = [&](const void* ptr) { return view(ptr, PO_BF16, m, m, B.ldm); };
   int cur = 0;
-  for (int it = 0; it < steps; ++it) {
+  for (int it = 0; it < steps;) {
     const Prec pr = prec_of(it);
+    const int gsz = group_at(it);
+    const int it_next = it + gsz;
     const bool from_g = direct && it == 0;
     OpView X = pr == P_TF32 ? op_view(pr, B.xt[cur], nullptr, rows, cols, B.ldx)
                             : op_view(pr, B.xb[cur], B.xl[cur], rows, cols, B.ldx);
@@ -311,30 +362,116 @@ int ns_core(const void* G, int dtype, long long batch, long long rows, long long
     add_op_outputs(g.epi, pr, a_hi, a_lo, B.ldm, ms, ds);
     if ((r = launch_gemm(g, s))) return r;
 
-    // B = b A + c A A
-    GemmDesc q;
-    set_kind(q, pr);
-    q.M = q.N = q.K = static_cast<int>(m);
-    q.batch = static_cast<int>(batch);
-    q.a[0] = Aop.v[0]; q.a[1] = Aop.v[1];
-    q.b[0] = Aop.v[0]; q.b[1] = Aop.v[1];
-    q.tri = true;
-    q.pair = g.pair;  // same tiling as the Gram, whose fp32 A holds only those tiles
-    q.sched = B.sched;
-    q.epi.alpha = c;
-    q.epi.mirror_same = 1;  // A is stored exactly symmetric by the Gram's mirrored stores
-    q.epi.nin = 1;
-    q.epi.in[0] = epi_in(B.af, IN_F32, B.ldm, ms, b);
-    if (ds) {
-      // A A = F F + D A + A D - D^2 with F (the operands) zero on the diagonal,
-      // D = diag(A) as the Gram wrote it; one row read of A.
-      q.epi.dsym = B.adiag;
-      q.epi.dsym_bs = m;
-      q.epi.diag_out = B.bdiag;
-      q.epi.diag_out_bs = m;
+    // The update's operand: B (one step) or the group's product Q.
+    OpView Uop = Bop;
+    const float* ucoef = B.bdiag;
+    float ubeta = a;
+    if (gsz == 1) {
+      // B = b A + c A A
+      GemmDesc q;
+      set_kind(q, pr);
+      q.M = q.N = q.K = static_cast<int>(m);
+      q.batch = static_cast<int>(batch);
+      q.a[0] = Aop.v[0]; q.a[1] = Aop.v[1];
+      q.b[0] = Aop.v[0]; q.b[1] = Aop.v[1];
+      q.tri = true;
+      q.pair = g.pair;  // same tiling as the Gram, whose fp32 A holds only those tiles
+      q.sched = B.sched;
+      q.epi.alpha = c;
+      q.epi.mirror_same = 1;  // A is stored exactly symmetric by the Gram's mirrored stores
+      q.epi.nin = 1;
+      q.epi.in[0] = epi_in(B.af, IN_F32, B.ldm, ms, b);
+      if (ds) {
+        // A A = F F + D A + A D - D^2 with F (the operands) zero on the diagonal,
+        // D = diag(A) as the Gram wrote it; one row read of A.
+        q.epi.dsym = B.adiag;
+        q.epi.dsym_bs = m;
+        q.epi.diag_out = B.bdiag;
+        q.epi.diag_out_bs = m;
+      }
+      add_op_outputs(q.epi, pr, b_hi, b_lo, B.ldm, ms, ds);
+      if ((r = launch_gemm(q, s))) return r;
+    } else {
+      // A_j: (FA[ia], dA[ia]) with its fp32 master in af (lower tiles);
+      // P_j = a I + B_j: (FP[ip], dP[ip]) with the constant a on the diagonal.
+      __nv_bfloat16* FA[2] = {reinterpret_cast<__nv_bfloat16*>(a_hi), reinterpret_cast<__nv_bfloat16*>(a_lo)};
+      float* dA[2] = {B.adiag, B.adiag2};
+      __nv_bfloat16* FP[2] = {reinterpret_cast<__nv_bfloat16*>(b_hi), reinterpret_cast<__nv_bfloat16*>(b_lo)};
+      float* dP[2] = {B.bdiag, B.bdiag2};
+      // B_j = b A_j + c A_j A_j (as the one-step square).
+      auto square = [&](const __nv_bfloat16* fa, const float* da, __nv_bfloat16* fb, float* db) -> int {
+        GemmDesc h;
+        set_kind(h, P_BF16);
+        h.M = h.N = h.K = static_cast<int>(m);
+        h.batch = static_cast<int>(batch);
+        h.a[0] = h.a[1] = bview(fa);
+        h.b[0] = h.b[1] = bview(fa);
+        h.tri = true;
+        h.pair = g.pair;
+        h.sched = B.sched;
+        h.epi.alpha = c;
+        h.epi.mirror_same = 1;
+        h.epi.nin = 1;
+        h.epi.in[0] = epi_in(B.af, IN_F32, B.ldm, ms, b);
+        h.epi.dsym = da;
+        h.epi.dsym_bs = m;
+        h.epi.diag_out = db;
+        h.epi.diag_out_bs = m;
+        add_op_outputs(h.epi, P_BF16, fb, nullptr, B.ldm, ms, true);
+        return launch_gemm(h, s);
+      };
+      // S T for split symmetric S, T (polynomials in A_j): operands F_S, F_T.
+      auto sprod = [&](const __nv_bfloat16* fs, const float* dsv, float ds_add, const __nv_bfloat16* ft,
+                       const float* dtv, float dt_add, __nv_bfloat16* fo, float* dout, float* f32_out) -> int {
+        GemmDesc h;
+        set_kind(h, P_BF16);
+        h.M = h.N = h.K = static_cast<int>(m);
+        h.batch = static_cast<int>(batch);
+        h.a[0] = h.a[1] = bview(fs);
+        h.b[0] = h.b[1] = bview(ft);
+        h.tri = true;
+        h.pair = g.pair;  // af's lower tiles are read by the next square on the same tiling
+        h.sched = B.sched;
+        h.epi.alpha = 1.0f;
+        h.epi.mirror_same = 1;
+        h.epi.s2_fs = epi_in(fs, IN_BF16, B.ldm, ms, 0.0f);
+        h.epi.s2_ft = epi_in(ft, IN_BF16, B.ldm, ms, 0.0f);
+        h.epi.s2_ds = dsv;
+        h.epi.s2_dt = dtv;
+        h.epi.s2_d_bs = m;
+        h.epi.s2_ds_add = ds_add;
+        h.epi.s2_dt_add = dt_add;
+        if (f32_out != nullptr) {
+          h.epi.out[h.epi.nout] = epi_out(f32_out, OUT_F32, B.ldm, ms);
+          h.epi.out[h.epi.nout++].lower_only = 1;
+        }
+        h.epi.diag_out = dout;
+        h.epi.diag_out_bs = m;
+        add_op_outputs(h.epi, P_BF16, fo, nullptr, B.ldm, ms, true);
+        return launch_gemm(h, s);
+      };
+      int ia = 0, ip = 1, iq = -1;
+      for (int j = 0; j < gsz; ++j) {
+        const int ipn = ip ^ 1;
+        if ((r = square(FA[ia], dA[ia], FP[ipn], dP[ipn]))) return r;
+        if (j >= 1) {
+          const int iqn = iq < 0 ? 0 : iq ^ 1;
+          if (j == 1) r = sprod(FP[ip], dP[ip], a, FP[ipn], dP[ipn], a, B.fq[iqn], B.qdiag[iqn], nullptr);
+          else r = sprod(B.fq[iq], B.qdiag[iq], 0.0f, FP[ipn], dP[ipn], a, B.fq[iqn], B.qdiag[iqn], nullptr);
+          if (r) return r;
+          iq = iqn;
+        }
+        if (j + 1 < gsz) {
+          if ((r = sprod(FP[ipn], dP[ipn], a, FP[ipn], dP[ipn], a, B.fp2, B.p2diag, nullptr))) return r;
+          if ((r = sprod(FA[ia], dA[ia], 0.0f, B.fp2, B.p2diag, 0.0f, FA[ia ^ 1], dA[ia ^ 1], B.af))) return r;
+          ia ^= 1;
+        }
+        ip = ipn;
+      }
+      Uop.v[0] = Uop.v[1] = bview(B.fq[iq]);
+      ucoef = B.qdiag[iq];
+      ubeta = 0.0f;
     }
-    add_op_outputs(q.epi, pr, b_hi, b_lo, B.ldm, ms, ds);
-    if ((r = launch_gemm(q, s))) return r;
 
     // Wide: X = a X + B X (B operand X stored [K = m][N = n], MN-major).
     // Tall: X = a X + X B (A operand X [n][K = m], K-major; B symmetric).
@@ -346,13 +483,13 @@ int ns_core(const void* G, int dtype, long long batch, long long rows, long long
       u.M = static_cast<int>(n);
       u.N = static_cast<int>(m);
       u.a[0] = X.v[0]; u.a[1] = X.v[1];
-      u.b[0] = Bop.v[0]; u.b[1] = Bop.v[1];
+      u.b[0] = Uop.v[0]; u.b[1] = Uop.v[1];
       u.a_kmajor = true;
       u.b_kmajor = true;
     } else {
       u.M = static_cast<int>(m);
       u.N = static_cast<int>(n);
-      u.a[0] = Bop.v[0]; u.a[1] = Bop.v[1];
+      u.a[0] = Uop.v[0]; u.a[1] = Uop.v[1];
       u.b[0] = X.v[0]; u.b[1] = X.v[1];
       u.b_kmajor = false;
     }
@@ -363,23 +500,23 @@ int ns_core(const void* G, int dtype, long long batch, long long rows, long long
       // s (B G or G B) + s (a + B_jj) G: both terms scaled by s = 1 / ||G||.
       u.epi.alpha_scale = B.scale;
       u.epi.in_scale = B.scale;
-      u.epi.in[0] = epi_in(G, IN_BF16, ld, bstride, a);
+      u.epi.in[0] = epi_in(G, IN_BF16, ld, bstride, ubeta);
     } else {
-      u.epi.in[0] = epi_in(B.xf, IN_F32, B.ldx, xs, a);
+      u.epi.in[0] = epi_in(B.xf, IN_F32, B.ldx, xs, ubeta);
     }
     if (ds) {
       // The dominant diagonal of B goes to the addend exactly: B X = F_B X +
       // diag(B) X (row scale a + B_ii) or X B = X F_B + X diag(B) (column scale).
       if (tall) {
-        u.epi.in0_colcoef = B.bdiag;
+        u.epi.in0_colcoef = ucoef;
         u.epi.in0_colcoef_bs = m;
       } else {
-        u.epi.in0_rowcoef = B.bdiag;
+        u.epi.in0_rowcoef = ucoef;
         u.epi.in0_rowcoef_bs = m;
       }
     }
-    if (it + 1 < steps) {
-      const Prec pn = prec_of(it + 1);
+    if (it_next < steps) {
+      const Prec pn = prec_of(it_next);
       const int nxt = cur ^ 1;
       u.epi.out[u.epi.nout++] = epi_out(B.xf, OUT_F32, B.ldx, xs);
       if (pn == P_TF32) add_op_outputs(u.epi, pn, B.xt[nxt], nullptr, B.ldx, xs);
@@ -404,6 +541,7 @@ int ns_core(const void* G, int dtype, long long batch, long long rows, long long
     }
     if ((r = launch_gemm(u, s))) return r;
     cur ^= 1;
+    it = it_next;
   }
   return PO_OK;
 }

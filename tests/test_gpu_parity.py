@@ -106,6 +106,26 @@ def test_ns_vs_oracle(cuda, shape, dtype, scale):
     assert _rel(_np(got), want) <= NS_TOL
 
 
+@pytest.mark.parametrize("shape,steps", [((512, 1536), 5), ((1536, 512), 5), ((320, 700), 2), ((700, 320), 3),
+                                         ((2, 384, 1024), 4), ((1024, 384), 6)])
+def test_ns_grouped_steps(cuda, shape, steps, monkeypatch):
+    """Matrices with n >= 2m (m >= 256) run their steps in groups of up to
+    three (one tall Gram and one tall update per group, the steps in between
+    as m x m products): within the NS tolerance of the oracle, and of the
+    one-step-at-a-time schedule (PO_NS_GROUP=0) for 2 .. 6 steps."""
+    g = torch.Generator().manual_seed(sum(shape) + steps)
+    Gc = (torch.randn(*shape, generator=g) * 0.02).bfloat16()
+    want = O.newton_schulz(_np(Gc), steps, out_bf16=True)
+    G = Gc.to(cuda)
+    got = native.newton_schulz_orthogonalize(G, steps, 3.4445, -4.7750, 2.0315, 1e-7)
+    monkeypatch.setenv("PO_NS_GROUP", "0")
+    one = native.newton_schulz_orthogonalize(G, steps, 3.4445, -4.7750, 2.0315, 1e-7)
+    monkeypatch.delenv("PO_NS_GROUP")
+    e_group, e_one, e_between = _rel(_np(got), want), _rel(_np(one), want), _rel(_np(got), _np(one))
+    print(f"NS {tuple(shape)} x{steps}: grouped {e_group:.2e}, one step at a time {e_one:.2e}, between {e_between:.2e}")
+    assert e_group <= NS_TOL and e_one <= NS_TOL and e_between <= NS_TOL
+
+
 def test_ns_noncontiguous_and_zero_and_steps0(cuda):
     G = torch.randn(96, 64, device=cuda).T  # non-contiguous view
     want = O.newton_schulz(_np(G.contiguous()))
