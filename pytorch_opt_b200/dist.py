@@ -30,13 +30,29 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
-from .muon import MuonGroup, muon_group_step, muon_scale, ns_workspace_bytes
+from .muon import MuonGroup, muon_group_step, muon_scale, ns_launches, ns_step_groups, ns_workspace_bytes
 
 
 def ns_flops(rows: int, cols: int, steps: int = 5) -> float:
     """Dense Newton–Schulz FLOPs of one matrix: steps * (4 m^2 n + 2 m^3), m = min dim."""
     m, n = min(rows, cols), max(rows, cols)
     return float(steps) * (4.0 * m * m * n + 2.0 * m ** 3)
+
+
+def ns_executed_flops(rows: int, cols: int, steps: int = 5) -> float:
+    """FLOPs the tensor cores execute for one matrix under the library's
+    schedule (``ns_step_groups``): symmetric m x m results count their lower
+    tiles only (256-wide tiles from m = 512, else 128), the full-matrix Gram
+    and update count once per step group."""
+    m, n = min(rows, cols), max(rows, cols)
+    t = 256 if m >= 512 else 128
+    k = -(-m // t)
+    tri = (k * (k + 1) / 2) / (k * k)
+    gram, small, update = 2.0 * m * m * n * tri, 2.0 * m ** 3 * tri, 2.0 * m * m * n
+    total = 0.0
+    for g in ns_step_groups(rows, cols, steps):
+        total += gram + update + (g + 3 * (g - 1)) * small
+    return total
 
 
 def lpt_assign(costs: list[float], world: int) -> list[list[int]]:
@@ -410,8 +426,8 @@ class ShardedMuon:
         """Kernels this library launches per local step (the all-gather is NCCL's)."""
         total = 0
         for g in self.groups:
-            count = g.params.shape[0] if self.compute is None else g[0].shape[0]
-            total += (-(-count // 32)) * (2 + 3 * int(self.hp["ns_steps"]))
+            count, rows, cols = g.params.shape if self.compute is None else g[0].shape
+            total += (-(-count // 32)) * ns_launches(rows, cols, int(self.hp["ns_steps"]))
         return total
 
     def local_update_sq(self) -> float:

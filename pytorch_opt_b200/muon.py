@@ -62,6 +62,30 @@ class MuonGroup:
             self.momentum = torch.zeros_like(self.params)
 
 
+def ns_step_groups(rows: int, cols: int, steps: int) -> list[int]:
+    """Step groups of the library's Newton-Schulz schedule (bf16 products):
+    matrices with min dim m >= 256 and max dim >= 2m run their steps in groups
+    of up to three (one Gram and one update of the full matrix per group),
+    unless PO_NS_GROUP=0; every other matrix one step at a time."""
+    m, n = min(rows, cols), max(rows, cols)
+    if steps <= 0:
+        return []
+    if m < 256 or n < 2 * m or os.environ.get("PO_NS_GROUP", "1") == "0":
+        return [1] * steps
+    groups, left = [], steps
+    while left > 0:
+        groups.append(min(3, left))
+        left -= groups[-1]
+    return groups
+
+
+def ns_launches(rows: int, cols: int, steps: int) -> int:
+    """Kernels one fused Muon call launches: the momentum pass, the scale
+    kernel and the products (a group of g >= 2 steps: one Gram, one update,
+    g squares and 3 (g - 1) products of m x m matrices; a single step: 3)."""
+    return 2 + sum(3 if g == 1 else 2 + g + 3 * (g - 1) for g in ns_step_groups(rows, cols, steps))
+
+
 def ns_workspace_bytes(count: int, rows: int, cols: int, max_batch: int = 32, dtype=torch.bfloat16) -> int:
     """Workspace one ``muon_group_step`` call needs (fused steps of up to ``max_batch`` matrices)."""
     return int(_lib.load().po_muon_step_workspace_bytes(min(count, max_batch), rows, cols, _lib.DTYPE_CODE[dtype]))
@@ -186,8 +210,8 @@ class GroupedMuon:
         matrices, the momentum pass, the scale (or packing) kernel and the products."""
         total = 0
         for g in self.groups:
-            chunks = -(-g.params.shape[0] // 32)
-            total += chunks * (2 + 3 * int(self.hp["ns_steps"]))
+            count, rows, cols = g.params.shape
+            total += -(-count // 32) * ns_launches(rows, cols, int(self.hp["ns_steps"]))
         return total
 
     def update_rms(self) -> float:
