@@ -510,12 +510,12 @@ def run_ours(args, rank, world, local_rank):
         if wait_profile is not None:
             line["gemm_wait_profile"] = wait_profile
         if world > 1:
-            fl = [layout.flops(r) / 1e12 for r in range(world)]
+            fl = [sum(ns_executed_flops(*shapes[i]) for i in layout.assign[r]) / 1e12 for r in range(world)]
             line["scaling_detail"] = {
                 "rank_step_ms": [round(x, 2) for x in step_ranks],
                 "rank_ns_compute_ms": [round(x, 2) for x in ns_ranks],
                 "rank_exposed_exchange_ms": [round(x, 2) for x in tail_ranks],
-                "rank_tflop": [round(x, 2) for x in fl],
+                "rank_executed_tflop": [round(x, 2) for x in fl],
                 "lpt_imbalance_max_over_mean": round(max(fl) / (sum(fl) / len(fl)), 4),
                 "exchange_chunks": layout.chunks,
                 "how": "per rank: CUDA-event time of its Newton-Schulz calls, and of the wait for the all-gathers "

@@ -96,14 +96,15 @@ def chunk_shares(chunks: int) -> list[float]:
 
 
 def bytes_per_flop(rows: int, cols: int) -> float:
-    """Exchanged bytes (bf16) per Newton–Schulz FLOP of a matrix: ~1/(10 min dim)."""
-    return 2.0 * rows * cols / ns_flops(rows, cols)
+    """Exchanged bytes (bf16) per executed Newton–Schulz FLOP of a matrix."""
+    return 2.0 * rows * cols / ns_executed_flops(rows, cols)
 
 
-# Pinned host-to-device copy rate over the fused Muon step's FLOP rate on one
-# B200 (about 50 GB/s against about 1.4 PFLOP/s): a batch whose gradient bytes
-# per NS FLOP exceed this copies longer than it computes.
-H2D_BYTES_PER_FLOP = 50e9 / 1.4e15
+# Pinned host-to-device copy rate over the fused Muon step's rate of executed
+# FLOPs on one B200 (about 50 GB/s against about 1.0 PFLOP/s executed): a
+# batch whose gradient bytes per executed NS FLOP exceed this copies longer
+# than it computes.
+H2D_BYTES_PER_FLOP = 50e9 / 1.0e15
 
 
 def host_copy_jobs(chunks: list, max_batch: int = 32,
@@ -127,7 +128,7 @@ def host_copy_jobs(chunks: list, max_batch: int = 32,
         per = []
         for k, count, rows, cols, es in groups:
             a = float(rows * cols * es)
-            b = ns_flops(rows, cols) * bytes_per_flop
+            b = ns_executed_flops(rows, cols) * bytes_per_flop
             per.append((k, count, a, b))
         order = sorted((g for g in per if g[2] < g[3]), key=lambda g: (g[2], g[0])) + \
             sorted((g for g in per if g[2] >= g[3]), key=lambda g: (-g[3], g[0]))
@@ -166,7 +167,9 @@ class ShardLayout:
                  chunks: int | None = None):
         self.shapes = [tuple(s) for s in shapes]
         self.world = world
-        costs = [ns_flops(r, c, steps) for r, c in self.shapes]
+        # Costs are the FLOPs the kernels execute (grouped steps make far-from-
+        # square matrices cheaper than the dense formula says).
+        costs = [ns_executed_flops(r, c, steps) for r, c in self.shapes]
         self.assign = lpt_assign(costs, world)
         if chunks is None:
             chunks = 1 if world == 1 else 4

@@ -177,7 +177,7 @@ def test_host_copy_jobs_expose_only_the_first_matrix_copy():
     lead) cover every matrix once, and in a copy-then-compute flow shop with
     the Llama-3-8B groups only the first (one-matrix) copy is left without
     compute to hide it."""
-    from pytorch_opt_b200.dist import H2D_BYTES_PER_FLOP, host_copy_jobs, ns_flops
+    from pytorch_opt_b200.dist import H2D_BYTES_PER_FLOP, host_copy_jobs, ns_executed_flops as ns_flops
     groups = [(0, 64, 4096, 4096, 2), (1, 64, 1024, 4096, 2), (2, 64, 14336, 4096, 2), (3, 32, 4096, 14336, 2)]
     for split in ([groups], [groups[:2], groups[2:]]):
         jobs = [j for c in host_copy_jobs(split) for j in c]
