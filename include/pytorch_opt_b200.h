@@ -83,7 +83,12 @@ int po_selftest_wait_timeout(unsigned long long limit_ns, int sleeping, void* st
  * fp32 by the epilogues ("diagonal split"); m < 256: split-bf16 pairs
  * (hi*hi + hi*lo + lo*hi) on every step. tf32_tail >= 0 runs the last
  * `tf32_tail` steps on tf32 products and the others on bf16 (both with the
- * diagonal split).
+ * diagonal split). With bf16 products on every step (default schedule or
+ * tf32_tail = 0), m >= 256 and max(rows, cols) >= 2m, the steps run in
+ * groups of up to three: one Gram and one update of the full matrix per
+ * group, the steps in between as m x m products (the next Gram is
+ * A P^2 for P = a I + b A + c A^2, the update applies P_0 P_1 ...);
+ * PO_NS_GROUP=0 in the environment runs one step at a time.
  * ---------------------------------------------------------------------- */
 size_t po_ns_workspace_bytes(long long batch, long long rows, long long cols);
 int po_newton_schulz(const void* G, int dtype, long long batch, long long rows, long long cols, long long ld,
