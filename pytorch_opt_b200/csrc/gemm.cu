@@ -286,6 +286,12 @@ int launch_gemm(const GemmDesc& d, cudaStream_t stream) {
   P.err = device_error_word();
   if (P.err == nullptr) return set_error(PO_ERR_CUDA, "device error word unavailable");
   P.prof = pair ? gemm_prof_word() : nullptr;
+  // The epilogue's L2 prefetch of the rows it reads is off: measured on the
+  // power-capped Llama step it cost 1-2 % (334-336 ms without, 338-339 ms
+  // with, same box). PO_GEMM_PREFETCH=1 in the environment turns it on (for
+  // measurement).
+  const char* pf_env = getenv("PO_GEMM_PREFETCH");
+  P.no_prefetch = (pf_env != nullptr && pf_env[0] == '1') ? 0 : 1;
   P.epi = d.epi;
 
   const bool a_mn = !d.a_kmajor, b_mn = !d.b_kmajor;

@@ -174,6 +174,7 @@ struct alignas(64) GemmParams {
   // Measurement only (nullable): cycles each role of the two-SM kernel spends
   // in its waits, summed over CTAs (see po_gemm_profile).
   unsigned long long* prof;
+  int no_prefetch;  // 1: no L2 prefetch of the epilogue's row reads (measurement)
   Epilogue epi;
 };
 
@@ -519,7 +520,7 @@ __device__ __forceinline__ void prefetch_row_segment(const void* base, int es, l
 // columns [col0, col0 + ncols) of `row`.
 __device__ __forceinline__ void epilogue_prefetch(const GemmParams& P, int b, int row, int col0, int ncols) {
   const Epilogue& E = P.epi;
-  if (row >= P.M) return;
+  if (row >= P.M || P.no_prefetch) return;
   ncols = min(ncols, P.N - col0);
 #pragma unroll
   for (int i = 0; i < kMaxEpiIn; ++i)
@@ -531,6 +532,11 @@ __device__ __forceinline__ void epilogue_prefetch(const GemmParams& P, int b, in
   if (E.diag_split) {
     prefetch_row_segment(E.dU.ptr, 4, E.dU.ld, E.dU.bstride, b, row, col0, ncols);
     prefetch_row_segment(E.dV.ptr, 4, E.dV.ld, E.dV.bstride, b, row, col0, ncols);
+  }
+  if (E.s2_ds != nullptr) {
+    prefetch_row_segment(E.s2_fs.ptr, 2, E.s2_fs.ld, E.s2_fs.bstride, b, row, col0, ncols);
+    if (E.s2_ft.ptr != E.s2_fs.ptr)
+      prefetch_row_segment(E.s2_ft.ptr, 2, E.s2_ft.ld, E.s2_ft.bstride, b, row, col0, ncols);
   }
 }
 
